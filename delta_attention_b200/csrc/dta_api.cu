@@ -1,0 +1,370 @@
+// extern "C" entry points of libdelta_attention_b200.so: argument validation,
+// workspace layout, TMA tensor-map encoding and kernel launches.  No entry
+// point allocates device memory; all scratch comes from the caller's workspace.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "delta_attention_b200.h"
+#include "dta_decode.h"
+#include "dta_prefill.h"
+
+namespace {
+
+thread_local int g_last_cuda_error = 0;
+
+constexpr size_t kHeaderBytes = 256;  // job counter, error word
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+inline int fail_cuda(cudaError_t e) {
+  g_last_cuda_error = (int)e;
+  return DTA_ERR_CUDA;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 4-D bf16 tensor map over (d, rows, heads, batch) with a 128-byte swizzle.
+int encode_4d(CUtensorMap* map, const void* base, int d, long long rows, int heads, int batch, long long s_row,
+              long long s_head, long long s_batch, int box_rows, int box_heads) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return DTA_ERR_CUDA;
+  cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)rows, (cuuint64_t)heads, (cuuint64_t)batch};
+  cuuint64_t strides[3] = {(cuuint64_t)(s_row * 2), (cuuint64_t)(s_head * 2), (cuuint64_t)(s_batch * 2)};
+  cuuint32_t box[4] = {64u, (cuuint32_t)box_rows, (cuuint32_t)box_heads, 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DTA_OK : DTA_ERR_CUDA;
+}
+
+struct DeviceInfo {
+  int ok = -1;
+  int sms = 0;
+};
+
+int check_device(int* sms) {
+  static DeviceInfo info[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e);
+  if (dev < 0 || dev >= 64) return DTA_ERR_UNSUPPORTED_DEVICE;
+  if (info[dev].ok < 0) {
+    int major = 0, n = 0;
+    if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+      return fail_cuda(e);
+    if ((e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return fail_cuda(e);
+    info[dev].ok = (major == 10) ? 1 : 0;
+    info[dev].sms = n;
+  }
+  if (!info[dev].ok) return DTA_ERR_UNSUPPORTED_DEVICE;
+  *sms = info[dev].sms;
+  return DTA_OK;
+}
+
+inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+inline bool stride_ok(long long s) { return s > 0 && (s * 2) % 16 == 0; }
+
+// ---------------------------------------------------------------------------
+// prefill layout
+// ---------------------------------------------------------------------------
+struct PrefillLayout {
+  int s_p, n_anchor, n_sel;
+  size_t buf_bytes;  // one of dense_buf / sparse_buf
+  size_t ws_bytes;
+};
+
+int prefill_layout(const dta_prefill_args* a, PrefillLayout* L) {
+  if (!a) return DTA_ERR_INVALID_ARG;
+  if (a->abi_version != DTA_ABI_VERSION) return DTA_ERR_INVALID_ARG;
+  if (a->batch <= 0 || a->n_heads <= 0 || a->n_kv_heads <= 0 || a->seq_len <= 0) return DTA_ERR_SHAPE;
+  if (a->head_dim != 64 && a->head_dim != 128) return DTA_ERR_HEAD_DIM;
+  if (a->n_heads % a->n_kv_heads != 0) return DTA_ERR_SHAPE;
+  const int G = a->n_heads / a->n_kv_heads;
+  if (G > 128 || 128 % G != 0) return DTA_ERR_SHAPE;
+  if (a->mode < 0 || a->mode > 2) return DTA_ERR_INVALID_ARG;
+  if (a->window < 0 || a->sink < 0 || a->q_block <= 0) return DTA_ERR_INVALID_ARG;
+  const int s = a->seq_len;
+  if (a->mode == DTA_MODE_SPARSE_ONLY) {
+    L->s_p = s;
+    L->n_anchor = 0;
+    L->n_sel = 0;
+  } else if (a->anchors) {
+    if (a->n_anchors <= 0 || a->s_p <= 0 || a->s_p > s) return DTA_ERR_INVALID_ARG;
+    L->s_p = a->s_p;
+    L->n_anchor = a->n_anchors;
+    L->n_sel = a->n_anchors + (s - a->s_p);
+  } else {
+    if (a->gamma <= 0) return DTA_ERR_GAMMA;
+    const int cut_n = s % a->gamma + (a->gamma > 128 ? a->gamma : 128);
+    const int s_p = s - cut_n;
+    if (s_p < 0 || s_p % a->gamma != 0) return DTA_ERR_GAMMA;
+    L->s_p = s_p;
+    L->n_anchor = s_p / a->gamma;
+    L->n_sel = L->n_anchor + cut_n;
+  }
+  const bool need_bufs = a->mode == DTA_MODE_DELTA && L->n_anchor > 0;
+  L->buf_bytes = need_bufs ? align_up((size_t)a->batch * L->n_anchor * a->n_heads * a->head_dim * 4, 256) : 0;
+  L->ws_bytes = kHeaderBytes + 2 * L->buf_bytes;
+  return DTA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dta_abi_version(void) { return DTA_ABI_VERSION; }
+
+int dta_last_cuda_error(void) { return g_last_cuda_error; }
+
+const char* dta_status_string(int st) {
+  switch (st) {
+    case DTA_OK: return "ok";
+    case DTA_ERR_INVALID_ARG: return "invalid argument";
+    case DTA_ERR_SHAPE: return "inconsistent shape";
+    case DTA_ERR_STRIDE: return "unsupported stride (head_dim must be contiguous, strides multiples of 16 bytes)";
+    case DTA_ERR_ALIGNMENT: return "pointer not 16-byte aligned";
+    case DTA_ERR_GAMMA: return "gamma incompatible with seq_len (s_p % gamma != 0 or seq_len < cut_n)";
+    case DTA_ERR_HEAD_DIM: return "head_dim not supported (64 or 128)";
+    case DTA_ERR_WORKSPACE: return "workspace missing or too small";
+    case DTA_ERR_CUDA: return "CUDA runtime error";
+    case DTA_ERR_UNSUPPORTED_DEVICE: return "device is not sm_100 (B200)";
+    case DTA_ERR_KERNEL_TIMEOUT: return "kernel gave up on a bounded wait";
+    default: return "unknown status";
+  }
+}
+
+size_t dta_prefill_workspace_size(const dta_prefill_args* a) {
+  PrefillLayout L;
+  if (prefill_layout(a, &L) != DTA_OK) return 0;
+  return L.ws_bytes;
+}
+
+int dta_prefill(const dta_prefill_args* a, void* stream_) {
+  PrefillLayout L;
+  int st = prefill_layout(a, &L);
+  if (st != DTA_OK) return st;
+  if (!a->q || !a->k || !a->v || !a->out) return DTA_ERR_INVALID_ARG;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out)) return DTA_ERR_ALIGNMENT;
+  if (!stride_ok(a->q_stride_s) || !stride_ok(a->q_stride_h) || !stride_ok(a->q_stride_b) ||
+      !stride_ok(a->k_stride_s) || !stride_ok(a->k_stride_h) || !stride_ok(a->k_stride_b) ||
+      !stride_ok(a->v_stride_s) || !stride_ok(a->v_stride_h) || !stride_ok(a->v_stride_b))
+    return DTA_ERR_STRIDE;
+  if (!a->workspace || a->workspace_bytes < L.ws_bytes || !aligned16(a->workspace)) return DTA_ERR_WORKSPACE;
+  if (a->anchor_delta && (a->mode != DTA_MODE_DELTA || !aligned16(a->anchor_delta))) return DTA_ERR_INVALID_ARG;
+  int sms = 0;
+  if ((st = check_device(&sms)) != DTA_OK) return st;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+
+  dta::PrefillParams p;
+  memset(&p, 0, sizeof(p));
+  const int B = a->batch, H = a->n_heads, Hkv = a->n_kv_heads, S = a->seq_len, d = a->head_dim;
+  const int G = H / Hkv, R = 128 / G;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(a->q);
+  p.q_sb = a->q_stride_b; p.q_sh = a->q_stride_h; p.q_ss = a->q_stride_s;
+  p.B = B; p.H = H; p.Hkv = Hkv; p.G = G; p.R = R;
+  p.scale_log2 = a->scaling * 1.4426950408889634f;
+  p.window = a->window; p.sink = a->sink; p.qblock = a->q_block;
+  p.gamma = a->gamma; p.s_p = L.s_p; p.n_anchor = L.n_anchor; p.n_sel = L.n_sel;
+  p.anchors = a->anchors;
+  p.mode = a->mode;
+  p.out_rows = S;
+  p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
+  p.counter = reinterpret_cast<int*>(ws);
+  p.error = reinterpret_cast<int*>(ws) + 1;
+  p.dense_buf = L.buf_bytes ? reinterpret_cast<float*>(ws + kHeaderBytes) : nullptr;
+  p.sparse_buf = L.buf_bytes ? reinterpret_cast<float*>(ws + kHeaderBytes + L.buf_bytes) : nullptr;
+
+  if ((st = encode_4d(&p.tm_k, a->k, d, S, Hkv, B, a->k_stride_s, a->k_stride_h, a->k_stride_b, 128, 1)) != DTA_OK)
+    return st;
+  if ((st = encode_4d(&p.tm_v, a->v, d, S, Hkv, B, a->v_stride_s, a->v_stride_h, a->v_stride_b, 128, 1)) != DTA_OK)
+    return st;
+  if ((st = encode_4d(&p.tm_q, a->q, d, S, H, B, a->q_stride_s, a->q_stride_h, a->q_stride_b, R, G)) != DTA_OK)
+    return st;
+
+  cudaError_t e = cudaMemsetAsync(a->workspace, 0, kHeaderBytes, stream);
+  if (e != cudaSuccess) return fail_cuda(e);
+
+  // launch 1: dense rows (anchors + tail) and sparse anchor rows
+  if (a->mode != DTA_MODE_SPARSE_ONLY && L.n_sel > 0) {
+    dta::PrefillParams r = p;
+    r.launch = dta::LAUNCH_ROWS;
+    r.direct_from = (a->mode == DTA_MODE_DELTA) ? L.n_anchor : 0;
+    r.n_dense_tiles = (L.n_sel + R - 1) / R;
+    r.n_sparse_tiles = (a->mode == DTA_MODE_DELTA) ? (L.n_anchor + R - 1) / R : 0;
+    r.n_jobs = (r.n_dense_tiles + r.n_sparse_tiles) * B * Hkv;
+    const int grid = r.n_jobs < sms ? r.n_jobs : sms;
+    if ((e = dta::launch_prefill(r, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
+  }
+  // launch 2: windowed rows [0, row_end) with the fused delta epilogue
+  {
+    dta::PrefillParams w = p;
+    w.launch = dta::LAUNCH_WINDOW;
+    w.row_end = (a->mode == DTA_MODE_SPARSE_ONLY) ? S : L.s_p;
+    w.n_window_tiles = (w.row_end + R - 1) / R;
+    w.n_jobs = w.n_window_tiles * B * Hkv;
+    if (w.n_jobs > 0) {
+      const int grid = w.n_jobs < sms ? w.n_jobs : sms;
+      if ((e = dta::launch_prefill(w, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
+    }
+  }
+  if (a->anchor_delta && L.buf_bytes) {
+    const long long n = (long long)B * L.n_anchor * H * d;
+    if ((e = dta::launch_anchor_delta(p.dense_buf, p.sparse_buf, a->anchor_delta, n, stream)) != cudaSuccess)
+      return fail_cuda(e);
+  }
+  return DTA_OK;
+}
+
+size_t dta_rows_workspace_size(const dta_rows_args* a) {
+  (void)a;
+  return kHeaderBytes;
+}
+
+int dta_rows(const dta_rows_args* a, void* stream_) {
+  if (!a || a->abi_version != DTA_ABI_VERSION) return DTA_ERR_INVALID_ARG;
+  if (a->batch <= 0 || a->n_heads <= 0 || a->n_kv_heads <= 0 || a->seq_len <= 0 || a->n_rows <= 0 ||
+      a->kv_len <= 0)
+    return DTA_ERR_SHAPE;
+  if (a->head_dim != 64 && a->head_dim != 128) return DTA_ERR_HEAD_DIM;
+  if (a->n_heads % a->n_kv_heads != 0) return DTA_ERR_SHAPE;
+  const int G = a->n_heads / a->n_kv_heads;
+  if (G > 128 || 128 % G != 0) return DTA_ERR_SHAPE;
+  if (!a->q || !a->k || !a->v || !a->out || !a->q_rows || !a->kv_limit) return DTA_ERR_INVALID_ARG;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out)) return DTA_ERR_ALIGNMENT;
+  if (!stride_ok(a->q_stride_s) || !stride_ok(a->q_stride_h) || !stride_ok(a->q_stride_b) ||
+      !stride_ok(a->k_stride_s) || !stride_ok(a->k_stride_h) || !stride_ok(a->k_stride_b) ||
+      !stride_ok(a->v_stride_s) || !stride_ok(a->v_stride_h) || !stride_ok(a->v_stride_b))
+    return DTA_ERR_STRIDE;
+  if (!a->workspace || a->workspace_bytes < kHeaderBytes || !aligned16(a->workspace)) return DTA_ERR_WORKSPACE;
+  int sms = 0, st;
+  if ((st = check_device(&sms)) != DTA_OK) return st;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  const int B = a->batch, H = a->n_heads, Hkv = a->n_kv_heads, d = a->head_dim, R = 128 / G;
+  dta::PrefillParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = reinterpret_cast<const __nv_bfloat16*>(a->q);
+  p.q_sb = a->q_stride_b; p.q_sh = a->q_stride_h; p.q_ss = a->q_stride_s;
+  p.B = B; p.H = H; p.Hkv = Hkv; p.G = G; p.R = R;
+  p.scale_log2 = a->scaling * 1.4426950408889634f;
+  p.window = 0; p.sink = 0; p.qblock = 64;
+  p.gamma = 1; p.s_p = 0; p.n_anchor = 0; p.n_sel = a->n_rows;
+  p.q_rows = a->q_rows;
+  p.kv_limit = a->kv_limit;
+  p.mode = DTA_MODE_RECOMPUTE;
+  p.launch = dta::LAUNCH_ROWS;
+  p.direct_from = 0;
+  p.out_by_list = 1;
+  p.out_rows = a->n_rows;
+  p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
+  p.counter = reinterpret_cast<int*>(ws);
+  p.error = reinterpret_cast<int*>(ws) + 1;
+  p.n_dense_tiles = (a->n_rows + R - 1) / R;
+  p.n_jobs = p.n_dense_tiles * B * Hkv;
+  if ((st = encode_4d(&p.tm_k, a->k, d, a->kv_len, Hkv, B, a->k_stride_s, a->k_stride_h, a->k_stride_b, 128, 1)) !=
+      DTA_OK)
+    return st;
+  if ((st = encode_4d(&p.tm_v, a->v, d, a->kv_len, Hkv, B, a->v_stride_s, a->v_stride_h, a->v_stride_b, 128, 1)) !=
+      DTA_OK)
+    return st;
+  cudaError_t e = cudaMemsetAsync(a->workspace, 0, kHeaderBytes, stream);
+  if (e != cudaSuccess) return fail_cuda(e);
+  const int grid = p.n_jobs < sms ? p.n_jobs : sms;
+  if ((e = dta::launch_prefill(p, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
+  return DTA_OK;
+}
+
+static int decode_setup(const dta_decode_args* a, dta::DecodeParams* p) {
+  if (!a || a->abi_version != DTA_ABI_VERSION) return DTA_ERR_INVALID_ARG;
+  if (a->batch <= 0 || a->n_heads <= 0 || a->n_kv_heads <= 0 || a->n_keys <= 0) return DTA_ERR_SHAPE;
+  if (a->head_dim != 64 && a->head_dim != 128) return DTA_ERR_HEAD_DIM;
+  if (a->n_heads % a->n_kv_heads != 0 || a->n_heads / a->n_kv_heads > 8) return DTA_ERR_SHAPE;
+  if (a->window < 0 || a->sink < 0) return DTA_ERR_INVALID_ARG;
+  memset(p, 0, sizeof(*p));
+  const int n = a->n_keys, C = dta::DEC_CHUNK;
+  p->B = a->batch; p->H = a->n_heads; p->Hkv = a->n_kv_heads; p->G = a->n_heads / a->n_kv_heads;
+  p->n_keys = n;
+  p->scale_log2 = a->scaling * 1.4426950408889634f;
+  p->window = a->window; p->sink = a->sink;
+  p->all_sparse = (n <= a->sink + a->window) ? 1 : 0;
+  p->want_dense = a->dense_out ? 1 : 0;
+  p->n_chunks = (n + C - 1) / C;
+  const int sink_keys = a->sink < n ? a->sink : n;
+  p->n_sink_chunks = (sink_keys + C - 1) / C;
+  int fw = (n - a->window) / C;
+  if (fw < p->n_sink_chunks) fw = p->n_sink_chunks;
+  p->first_window_chunk = fw;
+  if (p->want_dense || p->all_sparse) p->n_launched = p->n_chunks;
+  else p->n_launched = p->n_sink_chunks + (p->n_chunks - fw);
+  return DTA_OK;
+}
+
+size_t dta_decode_workspace_size(const dta_decode_args* a) {
+  dta::DecodeParams p;
+  if (decode_setup(a, &p) != DTA_OK) return 0;
+  return align_up((size_t)a->batch * a->n_heads * p.n_chunks * (4 + 2 * a->head_dim) * 4, 256);
+}
+
+int dta_decode(const dta_decode_args* a, void* stream_) {
+  dta::DecodeParams p;
+  int st = decode_setup(a, &p);
+  if (st != DTA_OK) return st;
+  if (!a->q || !a->k || !a->v || (!a->dense_out && !a->sparse_out)) return DTA_ERR_INVALID_ARG;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v)) return DTA_ERR_ALIGNMENT;
+  if ((a->dense_out && !aligned16(a->dense_out)) || (a->sparse_out && !aligned16(a->sparse_out)))
+    return DTA_ERR_ALIGNMENT;
+  if (!stride_ok(a->q_stride_h) || !stride_ok(a->q_stride_b) || !stride_ok(a->k_stride_s) ||
+      !stride_ok(a->k_stride_h) || !stride_ok(a->k_stride_b) || !stride_ok(a->v_stride_s) ||
+      !stride_ok(a->v_stride_h) || !stride_ok(a->v_stride_b))
+    return DTA_ERR_STRIDE;
+  const size_t need = dta_decode_workspace_size(a);
+  if (!a->workspace || a->workspace_bytes < need || !aligned16(a->workspace)) return DTA_ERR_WORKSPACE;
+  int sms = 0;
+  if ((st = check_device(&sms)) != DTA_OK) return st;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(a->q);
+  p.q_sb = a->q_stride_b; p.q_sh = a->q_stride_h;
+  p.k = reinterpret_cast<const __nv_bfloat16*>(a->k);
+  p.k_sb = a->k_stride_b; p.k_sh = a->k_stride_h; p.k_ss = a->k_stride_s;
+  p.v = reinterpret_cast<const __nv_bfloat16*>(a->v);
+  p.v_sb = a->v_stride_b; p.v_sh = a->v_stride_h; p.v_ss = a->v_stride_s;
+  p.partials = reinterpret_cast<float*>(a->workspace);
+  p.dense_out = reinterpret_cast<__nv_bfloat16*>(a->dense_out);
+  p.sparse_out = reinterpret_cast<__nv_bfloat16*>(a->sparse_out);
+  cudaError_t e = dta::launch_decode(p, a->head_dim, reinterpret_cast<cudaStream_t>(stream_));
+  if (e != cudaSuccess) return fail_cuda(e);
+  return DTA_OK;
+}
+
+int dta_check_workspace(const void* workspace, void* stream_, int* kernel_code) {
+  if (!workspace) return DTA_ERR_INVALID_ARG;
+  int word = 0;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  cudaError_t e = cudaMemcpyAsync(&word, reinterpret_cast<const int*>(workspace) + 1, sizeof(int),
+                                  cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess) return fail_cuda(e);
+  if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return fail_cuda(e);
+  if (kernel_code) *kernel_code = word;
+  return word == 0 ? DTA_OK : DTA_ERR_KERNEL_TIMEOUT;
+}
+
+}  // extern "C"

@@ -1,0 +1,681 @@
+// Delta-attention prefill on sm_100a: one persistent, warp-specialised
+// attention kernel used in two launches per layer.
+//
+//   launch "rows"   : key-dense causal attention for an explicit list of query
+//                     rows (anchors + dense tail; the qsa_kernel contract of
+//                     delta_attention/delta_kernel.py:57-70) and key-sparse
+//                     attention for the anchor rows (needed to form the delta).
+//                     Jobs are ordered longest-first and fetched from an atomic
+//                     counter, so the triangular work of the anchor rows
+//                     balances over the SMs without split-K.
+//   launch "window" : key-sparse attention (sink + block-anchored sliding
+//                     window, delta_attention/train/flex_delta.py:59-61) for
+//                     every row below s_p, with the delta correction of
+//                     delta_attention/llama.py:733-757 fused into the epilogue:
+//                     out = sparse + (dense[a] - sparse[a]) for the owning anchor
+//                     a.  The sparse output never goes to HBM.
+//
+// One CTA = 128 query rows (R rows x G heads of one KV group, R = 128 / G, so
+// the whole GQA group shares every K/V tile) against 128-key tiles:
+//   warp 0      : producer (job fetch, Q by TMA or cp.async gather, K/V by TMA)
+//   warp 1      : TMEM owner; lane 0 issues every tcgen05.mma and commit
+//   warps 2..5  : softmax + epilogue, one thread per query row (TMEM lane)
+// TMEM: S double buffer (2 x 128 columns fp32, P aliased as packed bf16 in the
+// first 64 columns of its S buffer), O accumulator (head_dim columns).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <cmath>
+#include <cstddef>
+
+#include "dta_ptx.cuh"
+#include "dta_prefill.h"
+
+namespace dta {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int NUM_THREADS = 192;
+constexpr int CTRL_BYTES = 1024;
+
+template <int HD>
+struct Geo {
+  static constexpr int REGIONS = HD / 64;           // 128-byte swizzle atoms along head_dim
+  static constexpr int REGION_BYTES = 128 * 128;    // 128 rows x 128 bytes
+  static constexpr int TILE_BYTES = REGIONS * REGION_BYTES;  // one 128 x HD bf16 tile
+  static constexpr int KV_STAGES = (HD == 128) ? 2 : 4;
+  static constexpr int Q_OFF = CTRL_BYTES;
+  static constexpr int KV_OFF = Q_OFF + 2 * TILE_BYTES;
+  static constexpr int SMEM_BYTES = KV_OFF + KV_STAGES * 2 * TILE_BYTES + 1024;  // + alignment slack
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int O_COL = 256;
+};
+
+// control block layout (byte offsets inside the 1024-byte control area)
+struct Ctrl {
+  uint64_t job_full[2], job_empty[2];
+  uint64_t q_full[2], q_empty[2];
+  uint64_t k_full[4], v_full[4], kv_empty[4];
+  uint64_t s_full[2], p_full[2];
+  uint64_t o_full, o_empty, drain;
+  int job[2][8];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block too large");
+
+enum JobKind : int { JOB_END = -1, JOB_WINDOW = 0, JOB_DENSE_ROWS = 1, JOB_SPARSE_ROWS = 2 };
+
+struct Job {
+  int kind, b, g, start, count, qmin, qmax, pad;
+};
+
+// ---------------------------------------------------------------------------
+// row lists and job decoding (identical in every role)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int list_q_row(const PrefillParams& p, int i) {
+  if (p.q_rows) return p.q_rows[i];
+  if (i < p.n_anchor) return p.anchors ? p.anchors[i] : i * p.gamma;
+  return p.s_p + (i - p.n_anchor);
+}
+__device__ __forceinline__ int list_kv_limit(const PrefillParams& p, int i) {
+  if (p.kv_limit) return p.kv_limit[i];
+  return list_q_row(p, i);
+}
+
+__device__ Job decode_job(const PrefillParams& p, int j) {
+  Job J;
+  J.pad = 0;
+  if (j >= p.n_jobs) {
+    J.kind = JOB_END;
+    J.b = J.g = J.start = J.count = J.qmin = J.qmax = 0;
+    return J;
+  }
+  if (p.launch == LAUNCH_WINDOW) {
+    const int nt = p.n_window_tiles;
+    const int bg = j / nt, t = j - bg * nt;
+    J.kind = JOB_WINDOW;
+    J.b = bg / p.Hkv;
+    J.g = bg - J.b * p.Hkv;
+    J.start = t * p.R;
+    J.count = min(p.R, p.row_end - J.start);
+    J.qmin = J.start;
+    J.qmax = J.start + J.count - 1;
+    return J;
+  }
+  const int BG = p.B * p.Hkv;
+  const int rank = j / BG, bg = j - (j / BG) * BG;
+  J.b = bg / p.Hkv;
+  J.g = bg - J.b * p.Hkv;
+  if (rank < p.n_dense_tiles) {
+    const int tile = p.n_dense_tiles - 1 - rank;  // longest (latest rows) first
+    J.kind = JOB_DENSE_ROWS;
+    J.start = tile * p.R;
+    J.count = min(p.R, p.n_sel - J.start);
+  } else {
+    const int tile = rank - p.n_dense_tiles;
+    J.kind = JOB_SPARSE_ROWS;
+    J.start = tile * p.R;
+    J.count = min(p.R, p.n_anchor - J.start);
+  }
+  J.qmin = list_kv_limit(p, J.start);
+  J.qmax = list_kv_limit(p, J.start + J.count - 1);
+  return J;
+}
+
+struct Plan {
+  int n0, n_tiles, sink_end, lo_min, lo_max;
+};
+
+__device__ __forceinline__ int block_window_lo(const PrefillParams& p, int t) {
+  const int bl = (t / p.qblock) * p.qblock + p.qblock - 1;
+  return max(0, bl - p.window + 1);
+}
+
+__device__ __forceinline__ Plan make_plan(const PrefillParams& p, const Job& J) {
+  Plan P;
+  if (J.kind == JOB_DENSE_ROWS) {
+    P.n0 = 0;
+    P.sink_end = 0;
+    P.lo_min = 0;
+    P.lo_max = 0;
+    P.n_tiles = (J.qmax + BN) / BN;
+  } else {
+    P.lo_min = block_window_lo(p, J.qmin);
+    P.lo_max = block_window_lo(p, J.qmax);
+    P.sink_end = min(p.sink, P.lo_min);
+    P.n0 = (P.sink_end + BN - 1) / BN;
+    P.n_tiles = P.n0 + (J.qmax - P.lo_min + BN) / BN;
+  }
+  return P;
+}
+__device__ __forceinline__ int tile_key_start(const Plan& P, int i) {
+  return i < P.n0 ? i * BN : P.lo_min + (i - P.n0) * BN;
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int HD>
+__global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
+  using G = Geo<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* base = smem_raw + (base_u32 - raw_u32);
+  Ctrl* ctrl = reinterpret_cast<Ctrl*>(base);
+  const uint32_t ctrl_u32 = base_u32;
+#define BAR(field) (ctrl_u32 + (uint32_t)offsetof(Ctrl, field))
+  const uint32_t q_u32 = base_u32 + G::Q_OFF;
+  const uint32_t kv_u32 = base_u32 + G::KV_OFF;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int* abort_flag = &ctrl->abort_flag;
+  int* err = p.error;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(BAR(job_full[0]) + 8 * i, 1);
+      mbar_init(BAR(job_empty[0]) + 8 * i, 5);  // MMA thread + 4 softmax warps
+      mbar_init(BAR(q_full[0]) + 8 * i, 1);
+      mbar_init(BAR(q_empty[0]) + 8 * i, 1);
+      mbar_init(BAR(s_full[0]) + 8 * i, 1);
+      mbar_init(BAR(p_full[0]) + 8 * i, 4);
+    }
+    for (int i = 0; i < G::KV_STAGES; ++i) {
+      mbar_init(BAR(k_full[0]) + 8 * i, 1);
+      mbar_init(BAR(v_full[0]) + 8 * i, 1);
+      mbar_init(BAR(kv_empty[0]) + 8 * i, 1);
+    }
+    mbar_init(BAR(o_full), 1);
+    mbar_init(BAR(o_empty), 4);
+    mbar_init(BAR(drain), 1);
+    ctrl->abort_flag = 0;
+    mbar_init_fence();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tm_k);
+    tma_prefetch_desc(&p.tm_v);
+    if (p.launch == LAUNCH_WINDOW) tma_prefetch_desc(&p.tm_q);
+  }
+  // Every warp must be converged at a CTA barrier (bar.sync counts whole
+  // warps) and at the warp-collective TMEM alloc/dealloc.
+  __syncwarp();
+  if (warp == 1) {
+    tmem_alloc(BAR(tmem_base), G::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctrl->tmem_base;
+
+  if (warp == 0) {
+    // ======================= producer =======================
+    int n = 0;  // global K/V tile counter
+    int issued_last_stage_n = -1;
+    for (int it = 0;; ++it) {
+      const int slot = it & 1;
+      int j;
+      if (p.launch == LAUNCH_WINDOW) {
+        j = blockIdx.x + it * gridDim.x;
+      } else {
+        int jj = 0;
+        if (lane == 0) jj = atomicAdd(p.counter, 1);
+        j = __shfl_sync(0xffffffffu, jj, 0);
+      }
+      if (!mbar_wait_warp(BAR(job_empty[0]) + 8 * slot, ((it >> 1) & 1) ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER))
+        break;
+      const Job J = decode_job(p, j);
+      if (lane == 0) {
+        int* dst = ctrl->job[slot];
+        dst[0] = J.kind; dst[1] = J.b; dst[2] = J.g; dst[3] = J.start;
+        dst[4] = J.count; dst[5] = J.qmin; dst[6] = J.qmax; dst[7] = 0;
+        mbar_arrive(BAR(job_full[0]) + 8 * slot);
+      }
+      if (J.kind == JOB_END) break;
+      // ---- Q tile (double-buffered across jobs) ----
+      const uint32_t qbuf = q_u32 + (uint32_t)(it & 1) * G::TILE_BYTES;
+      if (!mbar_wait_warp(BAR(q_empty[0]) + 8 * (it & 1), ((it >> 1) & 1) ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER))
+        break;
+      if (J.kind == JOB_WINDOW) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(BAR(q_full[0]) + 8 * (it & 1), G::TILE_BYTES);
+          for (int r = 0; r < G::REGIONS; ++r)
+            tma_load_4d(qbuf + r * G::REGION_BYTES, &p.tm_q, BAR(q_full[0]) + 8 * (it & 1), r * 64, J.start,
+                        J.g * p.G, J.b);
+        }
+      } else {
+        // gather 128 rows (R list rows x G heads) with cp.async into the
+        // 128-byte-swizzled K-major layout the MMA expects
+        constexpr int CH = HD / 8;  // 16-byte chunks per row
+        const __nv_bfloat16* qb = p.q + (long long)J.b * p.q_sb;
+        for (int c = lane; c < BM * CH; c += 32) {
+          const int m = c / CH, cc = c - (c / CH) * CH;
+          const int hh = m / p.R, rr = m - (m / p.R) * p.R;
+          const bool valid = rr < J.count;
+          const int row = valid ? list_q_row(p, J.start + rr) : 0;
+          const __nv_bfloat16* src =
+              qb + (long long)(J.g * p.G + hh) * p.q_sh + (long long)row * p.q_ss + cc * 8;
+          const int region = cc >> 3, cw = cc & 7;
+          const uint32_t dst = qbuf + region * G::REGION_BYTES + m * 128 + ((cw ^ (m & 7)) << 4);
+          cp_async_16(dst, src, valid ? 16u : 0u);
+        }
+        cp_async_wait_all();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BAR(q_full[0]) + 8 * (it & 1));
+      }
+      // ---- K/V tiles ----
+      const Plan P = make_plan(p, J);
+      bool ok = true;
+      for (int i = 0; i < P.n_tiles; ++i, ++n) {
+        const int st = n % G::KV_STAGES;
+        const uint32_t ph = (uint32_t)((n / G::KV_STAGES) & 1);
+        if (!mbar_wait_warp(BAR(kv_empty[0]) + 8 * st, ph ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const int ks = tile_key_start(P, i);
+          const uint32_t kdst = kv_u32 + (uint32_t)st * 2 * G::TILE_BYTES;
+          const uint32_t vdst = kdst + G::TILE_BYTES;
+          mbar_arrive_expect_tx(BAR(k_full[0]) + 8 * st, G::TILE_BYTES);
+          for (int r = 0; r < G::REGIONS; ++r)
+            tma_load_4d(kdst + r * G::REGION_BYTES, &p.tm_k, BAR(k_full[0]) + 8 * st, r * 64, ks, J.g, J.b);
+          mbar_arrive_expect_tx(BAR(v_full[0]) + 8 * st, G::TILE_BYTES);
+          for (int r = 0; r < G::REGIONS; ++r)
+            tma_load_4d(vdst + r * G::REGION_BYTES, &p.tm_v, BAR(v_full[0]) + 8 * st, r * 64, ks, J.g, J.b);
+        }
+        issued_last_stage_n = n;
+      }
+      if (!ok) break;
+    }
+    // On abort, let in-flight TMA loads land before the CTA can exit.
+    if (*abort_flag && lane == 0) {
+      for (int m = max(0, issued_last_stage_n - G::KV_STAGES + 1); m <= issued_last_stage_n; ++m) {
+        const int st = m % G::KV_STAGES;
+        const uint32_t ph = (uint32_t)((m / G::KV_STAGES) & 1);
+        volatile int never = 0;
+        long long t0 = clock64();
+        while (!(mbar_try_wait(BAR(k_full[0]) + 8 * st, ph) && mbar_try_wait(BAR(v_full[0]) + 8 * st, ph))) {
+          if (clock64() - t0 > kWaitTimeoutCycles || never) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ======================= MMA issuer =======================
+    if (lane == 0) {
+      constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, BN, 0);
+      constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, HD, 1);
+      const uint32_t tO = tmem + G::O_COL;
+      int n = 0;
+      bool have_pending = false, aborted = false;
+      int pend_n = 0, pend_stage = 0, pend_first = 0;
+      int jobs_pv = 0;  // number of jobs whose first PV has been issued
+
+      auto do_pv = [&](int m, int stage, int first) -> bool {
+        if (!mbar_wait(BAR(p_full[0]) + 8 * (m & 1), (m >> 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
+        if (first) {
+          if (jobs_pv > 0 &&
+              !mbar_wait(BAR(o_empty), (jobs_pv - 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+            return false;
+          ++jobs_pv;
+        }
+        if (!mbar_wait(BAR(v_full[0]) + 8 * stage, (m / G::KV_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+          return false;
+        tc_fence_after();
+        const uint32_t tP = tmem + (uint32_t)(m & 1) * 128;
+        const uint32_t vbase = kv_u32 + (uint32_t)stage * 2 * G::TILE_BYTES + G::TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t bdesc = smem_desc_sw128(vbase + kk * 2048, G::REGION_BYTES, 1024);
+          umma_ts(tO, tP + kk * 8, bdesc, IDESC_PV, (first && kk == 0) ? 0u : 1u);
+        }
+        umma_commit(BAR(kv_empty[0]) + 8 * stage);
+        umma_commit(BAR(o_full));
+        return true;
+      };
+
+      for (int it = 0;; ++it) {
+        const int slot = it & 1;
+        if (!mbar_wait(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) {
+          aborted = true;
+          break;
+        }
+        Job J;
+        {
+          const volatile int* src = ctrl->job[slot];
+          J.kind = src[0]; J.b = src[1]; J.g = src[2]; J.start = src[3];
+          J.count = src[4]; J.qmin = src[5]; J.qmax = src[6];
+        }
+        mbar_arrive(BAR(job_empty[0]) + 8 * slot);
+        if (J.kind == JOB_END) break;
+        const Plan P = make_plan(p, J);
+        const uint32_t qbuf = q_u32 + (uint32_t)(it & 1) * G::TILE_BYTES;
+        if (!mbar_wait(BAR(q_full[0]) + 8 * (it & 1), (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) {
+          aborted = true;
+          break;
+        }
+        for (int i = 0; i < P.n_tiles; ++i, ++n) {
+          const int st = n % G::KV_STAGES;
+          if (!mbar_wait(BAR(k_full[0]) + 8 * st, (n / G::KV_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tS = tmem + (uint32_t)(n & 1) * 128;
+          const uint32_t kbase = kv_u32 + (uint32_t)st * 2 * G::TILE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * G::REGION_BYTES + (kk & 3) * 32;
+            const uint64_t adesc = smem_desc_sw128(qbuf + off, 16, 1024);
+            const uint64_t bdesc = smem_desc_sw128(kbase + off, 16, 1024);
+            umma_ss(tS, adesc, bdesc, IDESC_QK, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(BAR(s_full[0]) + 8 * (n & 1));
+          if (i == P.n_tiles - 1) umma_commit(BAR(q_empty[0]) + 8 * (it & 1));
+          if (have_pending && !do_pv(pend_n, pend_stage, pend_first)) {
+            aborted = true;
+            break;
+          }
+          have_pending = true;
+          pend_n = n;
+          pend_stage = st;
+          pend_first = (i == 0);
+        }
+        if (aborted) break;
+      }
+      if (!aborted && have_pending) do_pv(pend_n, pend_stage, pend_first);
+      // drain: every issued tcgen05 op completes before TMEM is released
+      umma_commit(BAR(drain));
+      {
+        long long t0 = clock64();
+        while (!mbar_try_wait(BAR(drain), 0)) {
+          if (clock64() - t0 > kWaitTimeoutCycles) {
+            atomicCAS(err, 0, KERR_TIMEOUT_DRAIN);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ======================= softmax + epilogue =======================
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int r = quarter * 32 + lane;       // query row of this thread inside the tile
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int hh = r / p.R, rr = r - (r / p.R) * p.R;
+    const float sl2 = p.scale_log2;
+    int n = 0;
+    for (int it = 0;; ++it) {
+      const int slot = it & 1;
+      if (!mbar_wait_warp(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
+      Job J;
+      {
+        const volatile int* src = ctrl->job[slot];
+        J.kind = src[0]; J.b = src[1]; J.g = src[2]; J.start = src[3];
+        J.count = src[4]; J.qmin = src[5]; J.qmax = src[6];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(job_empty[0]) + 8 * slot);
+      if (J.kind == JOB_END) break;
+      const Plan P = make_plan(p, J);
+      const bool row_valid = rr < J.count;
+      int qpos;
+      if (J.kind == JOB_WINDOW) qpos = J.start + rr;
+      else qpos = row_valid ? list_kv_limit(p, J.start + rr) : J.qmax;
+      const bool sparse_kind = (J.kind != JOB_DENSE_ROWS);
+      const int lo_q = sparse_kind ? block_window_lo(p, qpos) : 0;
+      const int sink_q = sparse_kind ? p.sink : 0x7fffffff;
+
+      float m_run = -INFINITY, l_run = 0.f;
+      bool aborted = false;
+      for (int i = 0; i < P.n_tiles; ++i, ++n) {
+        if (!mbar_wait_warp(BAR(s_full[0]) + 8 * (n & 1), (n >> 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tS = tmem + lane_off + (uint32_t)(n & 1) * 128;
+        float s[BN];
+        {
+          uint32_t u[32];
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c) {
+            tmem_ld32(tS + c * 32, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(u[e]);
+          }
+        }
+        const int ks = tile_key_start(P, i);
+        const int seg_lo = (i < P.n0) ? 0 : P.lo_min;
+        const int seg_hi = (i < P.n0) ? P.sink_end : J.qmax + 1;  // exclusive
+        const bool full = (ks >= seg_lo) && (ks + BN <= seg_hi) && (ks + BN - 1 <= J.qmin) &&
+                          (!sparse_kind || ks + BN <= p.sink || ks >= P.lo_max);
+        float mt = -INFINITY;
+        if (full) {
+#pragma unroll
+          for (int e = 0; e < BN; ++e) mt = fmaxf(mt, s[e]);
+        } else {
+          const int A = seg_lo - ks;
+          const int Bq = min(seg_hi - 1, qpos) - ks;
+          const int X = sink_q - ks;
+          const int Y = lo_q - ks;
+#pragma unroll
+          for (int e = 0; e < BN; ++e) {
+            const bool v = (e >= A) && (e <= Bq) && !((e >= X) && (e < Y));
+            s[e] = v ? s[e] : -INFINITY;
+            mt = fmaxf(mt, s[e]);
+          }
+        }
+        mt *= sl2;  // scaled units (log2 domain); -inf stays -inf
+        if (i > 0) {
+          // PV of the previous tile must be complete before O is touched or P is released
+          if (!mbar_wait_warp(BAR(o_full), (n - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          // rescale only on a large max increase; the TMEM round trip is
+          // warp-collective, so lanes that do not need it scale by 1
+          const bool need = mt > m_run + 8.0f;
+          if (__any_sync(0xffffffffu, need)) {
+            const float alpha = !need ? 1.f : ((m_run == -INFINITY) ? 0.f : fast_exp2(m_run - mt));
+            const uint32_t tO = tmem + lane_off + G::O_COL;
+            uint32_t u[32];
+#pragma unroll
+            for (int c = 0; c < HD / 32; ++c) {
+              tmem_ld32(tO + c * 32, u);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
+              tmem_st32(tO + c * 32, u);
+            }
+            if (need) {
+              l_run *= alpha;
+              m_run = mt;
+            }
+          }
+        } else {
+          m_run = mt;
+        }
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        float lsum = 0.f;
+        __syncwarp();  // converge before the warp-collective TMEM stores
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = fast_exp2(fmaf(s[c * 32 + 2 * e], sl2, -m_use));
+            const float p1 = fast_exp2(fmaf(s[c * 32 + 2 * e + 1], sl2, -m_use));
+            lsum += p0 + p1;
+            pk[e] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(tS + c * 16, pk);
+        }
+        l_run += lsum;
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BAR(p_full[0]) + 8 * (n & 1));
+      }
+      if (aborted) break;
+      // ---- epilogue: wait for the last PV, normalise, correct, store ----
+      if (!mbar_wait_warp(BAR(o_full), (n - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
+      tc_fence_after();
+      const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
+      const int h = J.g * p.G + hh;
+      const uint32_t tO = tmem + lane_off + G::O_COL;
+      // destination of this row
+      // window: out[b, qpos, h, :] (bf16), rows < row_end, optionally + delta of owning anchor
+      // dense rows: list index < direct_from -> dense_buf fp32 ; else out[b, q_row, h, :] bf16
+      // sparse rows: sparse_buf fp32
+      const int li = J.start + rr;
+      bool store = row_valid;
+      int mode_out = 0;  // 0: bf16 to out, 1: fp32 to dense_buf, 2: fp32 to sparse_buf
+      long long out_row = 0;
+      const float* dlt_a = nullptr;
+      const float* dlt_b = nullptr;
+      if (J.kind == JOB_WINDOW) {
+        out_row = qpos;
+        if (store && p.mode == 0) {
+          int a;
+          if (p.anchors) {
+            int lo = 0, hi = p.n_anchor - 1;  // last anchor <= qpos (anchors[0] == 0)
+            while (lo < hi) {
+              const int mid = (lo + hi + 1) >> 1;
+              if (p.anchors[mid] <= qpos) lo = mid; else hi = mid - 1;
+            }
+            a = lo;
+          } else {
+            a = qpos / p.gamma;
+          }
+          const long long off = (((long long)J.b * p.n_anchor + a) * p.H + h) * HD;
+          dlt_a = p.dense_buf + off;
+          dlt_b = p.sparse_buf + off;
+        } else if (store && p.mode == 1) {
+          bool is_anchor;
+          if (p.anchors) {
+            int lo = 0, hi = p.n_anchor - 1;
+            while (lo < hi) {
+              const int mid = (lo + hi + 1) >> 1;
+              if (p.anchors[mid] <= qpos) lo = mid; else hi = mid - 1;
+            }
+            is_anchor = p.anchors[lo] == qpos;
+          } else {
+            is_anchor = (qpos % p.gamma) == 0;
+          }
+          store = !is_anchor;
+        }
+      } else if (J.kind == JOB_DENSE_ROWS) {
+        if (li < p.direct_from) {
+          mode_out = 1;
+        } else {
+          mode_out = 0;
+          out_row = !row_valid ? 0 : (p.out_by_list ? li : list_q_row(p, li));
+        }
+      } else {
+        mode_out = 2;
+      }
+      // TMEM reads are warp-collective: every lane loads, stores are predicated
+      __nv_bfloat16* dst_bf = (store && mode_out == 0)
+                                  ? p.out + (((long long)J.b * p.out_rows + out_row) * p.H + h) * HD
+                                  : nullptr;
+      float* dst_f = (store && mode_out != 0)
+                         ? (mode_out == 1 ? p.dense_buf : p.sparse_buf) +
+                               (((long long)J.b * p.n_anchor + li) * p.H + h) * HD
+                         : nullptr;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t u[32];
+        __syncwarp();  // stores below are per-lane; converge before the collective load
+        tmem_ld32(tO + c * 32, u);
+        tmem_wait_ld();
+        float o[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(u[e]) * inv_l;
+        if (dst_bf) {
+          if (dlt_a) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              const float4 da = *reinterpret_cast<const float4*>(dlt_a + c * 32 + e);
+              const float4 db = *reinterpret_cast<const float4*>(dlt_b + c * 32 + e);
+              o[e + 0] += da.x - db.x;
+              o[e + 1] += da.y - db.y;
+              o[e + 2] += da.z - db.z;
+              o[e + 3] += da.w - db.w;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 w;
+            w.x = pack_bf16x2(o[e + 0], o[e + 1]);
+            w.y = pack_bf16x2(o[e + 2], o[e + 3]);
+            w.z = pack_bf16x2(o[e + 4], o[e + 5]);
+            w.w = pack_bf16x2(o[e + 6], o[e + 7]);
+            *reinterpret_cast<uint4*>(dst_bf + c * 32 + e) = w;
+          }
+        } else if (dst_f) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(dst_f + c * 32 + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(o_empty));
+    }
+  }
+#undef BAR
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Geo<HD>::TMEM_COLS);
+  }
+}
+
+// anchor_delta[b, a, h, :] = dense_buf - sparse_buf (fp32), optional telemetry output
+__global__ void anchor_delta_kernel(const float* __restrict__ dense, const float* __restrict__ sparse,
+                                    float* __restrict__ out, long long n4) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(dense)[i];
+    const float4 b = reinterpret_cast<const float4*>(sparse)[i];
+    reinterpret_cast<float4*>(out)[i] = make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
+  }
+}
+
+template <int HD>
+static cudaError_t launch_prefill_hd(const PrefillParams& p, int grid, cudaStream_t stream) {
+  static bool attr_set = false;
+  const int smem = Geo<HD>::SMEM_BYTES;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  prefill_kernel<HD><<<grid, NUM_THREADS, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill(const PrefillParams& p, int head_dim, int grid, cudaStream_t stream) {
+  if (head_dim == 128) return launch_prefill_hd<128>(p, grid, stream);
+  return launch_prefill_hd<64>(p, grid, stream);
+}
+
+cudaError_t launch_anchor_delta(const float* dense, const float* sparse, float* out, long long n, cudaStream_t s) {
+  const long long n4 = n / 4;
+  int blocks = (int)((n4 + 255) / 256);
+  if (blocks > 4096) blocks = 4096;
+  if (blocks < 1) blocks = 1;
+  anchor_delta_kernel<<<blocks, 256, 0, s>>>(dense, sparse, out, n4);
+  return cudaGetLastError();
+}
+
+}  // namespace dta

@@ -1,0 +1,45 @@
+// Internal launch parameters of the prefill attention kernel (not part of the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace dta {
+
+enum Launch : int { LAUNCH_ROWS = 0, LAUNCH_WINDOW = 1 };
+
+struct PrefillParams {
+  CUtensorMap tm_q;  // (d, s, H, B), box (64, R, G, 1): window launch only
+  CUtensorMap tm_k;  // (d, s_kv, Hkv, B), box (64, 128, 1, 1)
+  CUtensorMap tm_v;
+  const __nv_bfloat16* q;
+  long long q_sb, q_sh, q_ss;  // element strides for the cp.async row gather
+  int B, H, Hkv, G, R;
+  float scale_log2;             // scaling * log2(e)
+  int window, sink, qblock;
+  int gamma, s_p, n_anchor, n_sel;
+  const int* anchors;           // optional explicit anchor rows (sorted)
+  const int* q_rows;            // optional explicit row list (rows launch)
+  const int* kv_limit;          // optional explicit key limits (rows launch)
+  int mode;                     // 0 delta, 1 recompute, 2 sparse-only
+  int launch;                   // Launch
+  int row_end;                  // window launch: rows [0, row_end) are produced
+  int direct_from;              // rows launch: list index from which dense rows go to `out`
+  int out_by_list;              // rows launch: out row = list index (dta_rows) instead of q row
+  int out_rows;                 // rows of `out` per batch
+  int n_dense_tiles, n_sparse_tiles, n_window_tiles;
+  int n_jobs;
+  int* counter;                 // job counter (rows launch), zeroed by the host
+  int* error;                   // kernel error word, zeroed by the host
+  float* dense_buf;             // [B, n_anchor, H, d] fp32
+  float* sparse_buf;            // [B, n_anchor, H, d] fp32
+  __nv_bfloat16* out;           // [B, out_rows, H, d]
+};
+
+cudaError_t launch_prefill(const PrefillParams& p, int head_dim, int grid, cudaStream_t stream);
+cudaError_t launch_anchor_delta(const float* dense, const float* sparse, float* out, long long n,
+                                cudaStream_t stream);
+
+}  // namespace dta

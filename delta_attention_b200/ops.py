@@ -1,0 +1,196 @@
+"""Torch-facing wrappers over the C ABI (device memory, streams and strides).
+
+Each op checks its inputs, sizes the caller-side workspace with the library's
+``*_workspace_size`` query, passes raw pointers plus the current CUDA stream,
+and raises :class:`DtaError` for any non-zero status.  There is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import ABI_VERSION, DecodeArgs, PrefillArgs, RowsArgs, check, lib
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _bf16_lastdim_contig(t: torch.Tensor) -> torch.Tensor:
+    if t.dtype != torch.bfloat16:
+        t = t.to(torch.bfloat16)
+    if t.stride(-1) != 1 or t.data_ptr() % 16 != 0 or any(
+            (s * 2) % 16 != 0 for s in t.stride()[:-1]):
+        t = t.contiguous()
+    return t
+
+
+def _strides(t: torch.Tensor):
+    """Element strides of the leading dims; size-1 dims get a harmless legal stride."""
+    out = []
+    for size, st in zip(t.shape[:-1], t.stride()[:-1]):
+        if size == 1 or st <= 0:
+            st = t.shape[-1]
+        out.append(int(st))
+    return out
+
+
+def _check_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("delta_attention_b200 ops take CUDA tensors (there is no CPU path)")
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, window: int, sink: int,
+            scaling: Optional[float] = None, mode: str = "delta", q_block: int = 64,
+            anchors: Optional[torch.Tensor] = None, s_p: Optional[int] = None,
+            return_anchor_delta: bool = False, workspace: Optional[torch.Tensor] = None):
+    """Delta-attention prefill of one layer.
+
+    q [b, H, s, d], k/v [b, Hkv, s, d] (post-RoPE; any strides with d
+    contiguous).  Returns ``out`` [b, s, H, d] in q's dtype (computation in
+    bf16, as the reference's sparse path does, ``delta_attention/llama.py:383-388``),
+    and, with ``return_anchor_delta``, the fp32 anchor deltas [b, n_anchor, H, d].
+    """
+    _check_cuda(q, k, v)
+    odt = q.dtype
+    qb, kb, vb = _bf16_lastdim_contig(q), _bf16_lastdim_contig(k), _bf16_lastdim_contig(v)
+    b, H, s, d = qb.shape
+    Hkv = kb.shape[1]
+    if kb.shape != (b, Hkv, s, d) or vb.shape != kb.shape:
+        raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
+    if scaling is None:
+        scaling = d ** -0.5
+    if mode not in _lib.MODES:
+        raise ValueError(f"unknown mode {mode!r}")
+    out = torch.empty(b, s, H, d, dtype=torch.bfloat16, device=q.device)
+    a = PrefillArgs()
+    a.abi_version = ABI_VERSION
+    a.batch, a.n_heads, a.n_kv_heads, a.seq_len, a.head_dim = b, H, Hkv, s, d
+    a.q = _ptr(qb)
+    a.q_stride_b, a.q_stride_h, a.q_stride_s = _strides(qb)
+    a.k = _ptr(kb)
+    a.k_stride_b, a.k_stride_h, a.k_stride_s = _strides(kb)
+    a.v = _ptr(vb)
+    a.v_stride_b, a.v_stride_h, a.v_stride_s = _strides(vb)
+    a.out = _ptr(out)
+    a.scaling = float(scaling)
+    a.gamma, a.window, a.sink, a.q_block = int(gamma), int(window), int(sink), int(q_block)
+    a.mode = _lib.MODES[mode]
+    anc = None
+    if anchors is not None:
+        anc = anchors.to(device=q.device, dtype=torch.int32).contiguous()
+        a.anchors = _ptr(anc)
+        a.n_anchors = anc.numel()
+        a.s_p = int(s_p)
+    ws_bytes = lib().dta_prefill_workspace_size(ctypes.byref(a))
+    if ws_bytes == 0:
+        # let dta_prefill report the precise validation status
+        check(lib().dta_prefill(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_prefill")
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = _workspace(ws_bytes, q.device)
+    a.workspace = _ptr(workspace)
+    a.workspace_bytes = workspace.numel()
+    delta = None
+    if return_anchor_delta and mode == "delta":
+        if anc is not None:
+            n_anchor = anc.numel()
+        else:
+            cut_n = s % gamma + max(128, gamma)
+            n_anchor = max(s - cut_n, 0) // gamma
+        delta = torch.empty(b, n_anchor, H, d, dtype=torch.float32, device=q.device)
+        a.anchor_delta = _ptr(delta)
+    check(lib().dta_prefill(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_prefill")
+    if odt != torch.bfloat16:
+        out = out.to(odt)
+    return (out, delta) if return_anchor_delta else out
+
+
+def rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_rows: torch.Tensor, kv_limit: torch.Tensor,
+         scaling: Optional[float] = None) -> torch.Tensor:
+    """Attention for a list of query rows: row i uses ``q[:, :, q_rows[i]]`` and
+    attends keys ``[0, kv_limit[i]]`` (non-decreasing).  Returns [b, n, H, d]
+    (the ``qsa_kernel`` contract, ``delta_attention/delta_kernel.py:259-329``)."""
+    _check_cuda(q, k, v)
+    odt = q.dtype
+    qb, kb, vb = _bf16_lastdim_contig(q), _bf16_lastdim_contig(k), _bf16_lastdim_contig(v)
+    b, H, sq, d = qb.shape
+    Hkv, skv = kb.shape[1], kb.shape[2]
+    if scaling is None:
+        scaling = d ** -0.5
+    qr = q_rows.to(device=q.device, dtype=torch.int32).contiguous()
+    kl = kv_limit.to(device=q.device, dtype=torch.int32).contiguous()
+    n = qr.numel()
+    out = torch.empty(b, n, H, d, dtype=torch.bfloat16, device=q.device)
+    a = RowsArgs()
+    a.abi_version = ABI_VERSION
+    a.batch, a.n_heads, a.n_kv_heads, a.seq_len, a.head_dim, a.n_rows = b, H, Hkv, sq, d, n
+    a.q = _ptr(qb)
+    a.q_stride_b, a.q_stride_h, a.q_stride_s = _strides(qb)
+    a.k = _ptr(kb)
+    a.k_stride_b, a.k_stride_h, a.k_stride_s = _strides(kb)
+    a.kv_len = skv
+    a.v = _ptr(vb)
+    a.v_stride_b, a.v_stride_h, a.v_stride_s = _strides(vb)
+    a.q_rows, a.kv_limit = _ptr(qr), _ptr(kl)
+    a.out = _ptr(out)
+    a.scaling = float(scaling)
+    ws = _workspace(lib().dta_rows_workspace_size(ctypes.byref(a)), q.device)
+    a.workspace, a.workspace_bytes = _ptr(ws), ws.numel()
+    check(lib().dta_rows(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_rows")
+    return out if odt == torch.bfloat16 else out.to(odt)
+
+
+def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, window: int, sink: int,
+           scaling: Optional[float] = None, want_dense: bool = True, want_sparse: bool = True,
+           n_keys: Optional[int] = None) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor]]:
+    """One decode row per (batch, head).  q [b, H, 1, d]; k/v [b, Hkv, n, d]
+    (only the first ``n_keys`` keys are used).  Returns ``(dense, sparse)``,
+    each [b, 1, H, d] bf16 or None; both come from one pass over the cache."""
+    _check_cuda(q, k, v)
+    qb, kb, vb = _bf16_lastdim_contig(q), _bf16_lastdim_contig(k), _bf16_lastdim_contig(v)
+    b, H, one, d = qb.shape
+    if one != 1:
+        raise ValueError("decode takes one query row per (batch, head)")
+    Hkv, n = kb.shape[1], kb.shape[2] if n_keys is None else int(n_keys)
+    if scaling is None:
+        scaling = d ** -0.5
+    dense = torch.empty(b, 1, H, d, dtype=torch.bfloat16, device=q.device) if want_dense else None
+    sparse = torch.empty(b, 1, H, d, dtype=torch.bfloat16, device=q.device) if want_sparse else None
+    a = DecodeArgs()
+    a.abi_version = ABI_VERSION
+    a.batch, a.n_heads, a.n_kv_heads, a.n_keys, a.head_dim = b, H, Hkv, n, d
+    a.q = _ptr(qb)
+    a.q_stride_b, a.q_stride_h = _strides(qb)[:2]
+    a.k = _ptr(kb)
+    a.k_stride_b, a.k_stride_h, a.k_stride_s = _strides(kb)
+    a.v = _ptr(vb)
+    a.v_stride_b, a.v_stride_h, a.v_stride_s = _strides(vb)
+    a.scaling = float(scaling)
+    a.window, a.sink = int(window), int(sink)
+    a.dense_out, a.sparse_out = _ptr(dense), _ptr(sparse)
+    ws = _workspace(lib().dta_decode_workspace_size(ctypes.byref(a)), q.device)
+    a.workspace, a.workspace_bytes = _ptr(ws), ws.numel()
+    check(lib().dta_decode(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_decode")
+    return dense, sparse
+
+
+def check_workspace(workspace: torch.Tensor) -> int:
+    """Synchronously read a workspace's kernel error word; raises on a timeout."""
+    code = ctypes.c_int(0)
+    st = lib().dta_check_workspace(ctypes.c_void_p(_ptr(workspace)), ctypes.c_void_p(_stream()),
+                                   ctypes.byref(code))
+    check(st, f"kernel error word {code.value}")
+    return code.value
