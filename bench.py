@@ -1,0 +1,457 @@
+#!/usr/bin/env python
+"""Delta-attention prefill throughput on B200 (the BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload (BASELINE.json config 2 at its headline point): one layer of delta
+attention with Llama-3.1-8B attention shapes -- 32 query / 8 KV heads,
+head_dim 128, N = 131072 tokens, window W = 2048, sink S = 128, stride
+gamma = 64, bf16 -- on seeded synthetic post-RoPE q/k/v (N(0,1)*0.5,
+RoPE theta 500000).  A step is one prefill of that layer.
+
+Multi-GPU (torchrun, one process per GPU, NCCL only for the barrier and the
+max-over-ranks timing): the work is partitioned by (sequence, KV group) unit
+(``delta_attention_b200.sharding``); with ``--scaling weak`` (default) the
+job holds one sequence per rank, so per-GPU work is fixed.
+
+Printed JSON line (rank 0): ``value`` = tokens/s over the whole job with
+inputs resident in HBM (inputs 1.6 GB per GPU > 126 MB L2, so no L2 flush);
+``roofline`` for the prefill kernel (analytic FLOPs 4*H*d*(N*(W+S) + (N/gamma)*N/2)
+over the live CUDA-event time of its launches, against MEASURED_PEAKS.json);
+``e2e`` = the same metric through the reference-facing plug-in
+(``DeltaAttention.delta_forward``) with pinned host inputs, host<->device
+copies inside the timed region; ``cpu_baseline`` = the CPU oracle on a
+bounded row sample of the same workload on this host's cores.
+``--impl reference`` times that CPU implementation as the reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "delta-attn prefill tokens/s/GPU @128K (Llama-3.1-8B shapes); % bf16 TC peak"
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--seq", type=int, default=131072)
+    ap.add_argument("--heads", type=int, default=32)
+    ap.add_argument("--kv-heads", type=int, default=8)
+    ap.add_argument("--head-dim", type=int, default=128)
+    ap.add_argument("--window", type=int, default=2048)
+    ap.add_argument("--sink", type=int, default=128)
+    ap.add_argument("--gamma", type=int, default=64)
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-clocks", action="store_true")
+    return ap.parse_args()
+
+
+def analytic_flops(H, d, N, W, S, gamma):
+    """north_star FLOP count: 4*H*d*(N*(W+S) + (N/gamma)*N/2), split by launch."""
+    window = 4.0 * H * d * N * (W + S)
+    rows = 4.0 * H * d * (N / gamma) * N / 2.0
+    return window + rows, window, rows
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, enabled: bool = True):
+        self.gpu = gpu_index
+        self.enabled = enabled
+        self.proc = None
+        self.out = ""
+
+    def __enter__(self):
+        if self.enabled:
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                     "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except OSError:
+                self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+        return False
+
+    def summary(self):
+        rows = [r for r in csv.reader(io.StringIO(self.out)) if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle on a bounded row sample
+# ---------------------------------------------------------------------------
+def cpu_sample_inputs(args, r0, R, seed=0):
+    """Seeded CPU inputs covering keys [0, r0+R) and query rows [r0, r0+R) of the workload."""
+    import torch
+    from delta_attention_b200.rope import apply_rope, cos_sin
+
+    H, Hkv, d = args.heads, args.kv_heads, args.head_dim
+    n = r0 + R
+    g = torch.Generator().manual_seed(seed)
+    q = torch.zeros(1, H, n, d)
+    q[:, :, r0:] = torch.randn(1, H, R, d, generator=g) * 0.5
+    k = torch.randn(1, Hkv, n, d, generator=g) * 0.5
+    v = torch.randn(1, Hkv, n, d, generator=g) * 0.5
+    cos, sin = cos_sin(torch.arange(n), d, 500000.0)
+    q = apply_rope(q, cos, sin).bfloat16()
+    k = apply_rope(k, cos, sin).bfloat16()
+    return q, k, v.bfloat16()
+
+
+def cpu_oracle_step(args, q, k, v, r0, R):
+    """One bounded CPU step: delta output of rows [r0, r0+R) (sparse rows plus
+    their anchors' dense and sparse rows), fp32, via the oracle."""
+    import torch
+    from oracle import delta_oracle as orc
+
+    rows = torch.arange(r0, r0 + R)
+    # the oracle needs the full sequence length for the layout; pad K/V views
+    return orc.delta_forward_rows(_PadSeq(q, args.seq), _PadSeq(k, args.seq), _PadSeq(v, args.seq), rows,
+                                  args.gamma, args.window, args.sink, dtype=torch.float32)
+
+
+class _PadSeq:
+    """View of a [b, h, n, d] tensor that reports sequence length ``s`` (>= n)
+    for layout purposes; only rows < n are ever indexed by the sample."""
+
+    def __init__(self, t, s):
+        self.t = t
+        self.shape = (t.shape[0], t.shape[1], s, t.shape[3])
+
+    def __getitem__(self, idx):
+        return self.t[idx]
+
+    def to(self, *a, **kw):
+        return self.t.to(*a, **kw)
+
+    def float(self):
+        return self
+
+
+def cpu_baseline(args, seconds):
+    """Time the oracle on a row sample near N/2 sized to ~``seconds`` of CPU work.
+    Returns (tokens/s, threads, description)."""
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    r0 = args.seq // 2
+    R = 256
+    q, k, v = cpu_sample_inputs(args, r0, 4096)
+    t0 = time.perf_counter()
+    cpu_oracle_step(args, q, k, v, r0, R)
+    t_small = time.perf_counter() - t0
+    R = int(max(256, min(4096, R * seconds / max(t_small, 1e-3))) // args.gamma * args.gamma)
+    t0 = time.perf_counter()
+    cpu_oracle_step(args, q, k, v, r0, R)
+    dt = time.perf_counter() - t0
+    desc = (f"oracle (torch CPU fp32) rows [{r0}, {r0 + R}) of the N={args.seq} layer, all {args.heads} heads, "
+            f"with their {R // args.gamma} anchors' dense and sparse rows; tokens/s = rows / time")
+    return R / dt, threads, desc
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    r0 = args.seq // 2
+    q, k, v = cpu_sample_inputs(args, r0, 4096)
+    budget = max(0.5, min(2.0, 150.0 / max(1, args.steps + args.warmup)))
+    t0 = time.perf_counter()
+    cpu_oracle_step(args, q, k, v, r0, 128)
+    t_small = time.perf_counter() - t0
+    R = int(max(args.gamma, min(4096, 128 * budget / max(t_small, 1e-3))) // args.gamma * args.gamma)
+    for _ in range(args.warmup):
+        cpu_oracle_step(args, q, k, v, r0, R)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        cpu_oracle_step(args, q, k, v, r0, R)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = R * args.steps / total
+    sample = (f"rows [{r0}, {r0 + R}) of the N={args.seq} layer per step (all {args.heads} heads, plus their "
+              f"{R // args.gamma} anchors' dense and sparse rows), CPU oracle port fp32")
+    line = {
+        "metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps,
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1)*0.5, RoPE theta 5e5)",
+        "config": workload_config(args, world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def physical_gpu(local_rank: int) -> str:
+    """nvidia-smi id of this process's GPU (honours CUDA_VISIBLE_DEVICES)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        if local_rank < len(ids):
+            return ids[local_rank]
+    return str(local_rank)
+
+
+def workload_config(args, world):
+    return {
+        "workload": "config2: single-layer delta-attention prefill, Llama-3.1-8B attention shapes",
+        "seq_len": args.seq, "n_heads": args.heads, "n_kv_heads": args.kv_heads, "head_dim": args.head_dim,
+        "window": args.window, "sink": args.sink, "gamma": args.gamma, "sequences_per_gpu":
+            (1 if args.scaling == "weak" else 1.0 / world), "partition": "kv-group units",
+        "l2": "inputs 1.6 GB per GPU exceed the 126 MB L2; no flush",
+    }
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from delta_attention_b200 import ops
+    from delta_attention_b200._lib import PHASE_ROWS, PHASE_WINDOW
+    from delta_attention_b200.sharding import job_for, owned_units
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    H, Hkv, d, N = args.heads, args.kv_heads, args.head_dim, args.seq
+    G = H // Hkv
+    n_seqs = job_for(args.scaling, world, Hkv)
+    units = owned_units(n_seqs, Hkv, world, rank)
+    U = len(units)
+    # this rank's units stacked along the batch axis: q [U, G, N, d], k/v [U, 1, N, d]
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    q = (torch.randn(U, G, N, d, generator=gen, device=dev, dtype=torch.float32) * 0.5)
+    k = (torch.randn(U, 1, N, d, generator=gen, device=dev, dtype=torch.float32) * 0.5)
+    v = (torch.randn(U, 1, N, d, generator=gen, device=dev, dtype=torch.float32) * 0.5).bfloat16()
+    from delta_attention_b200.rope import apply_rope, cos_sin
+    cos, sin = cos_sin(torch.arange(N, device=dev), d, 500000.0)
+    q = apply_rope(q, cos, sin).bfloat16()
+    k = apply_rope(k, cos, sin).bfloat16()
+    del cos, sin
+    out = torch.empty(U, N, G, d, dtype=torch.bfloat16, device=dev)
+    kw = dict(gamma=args.gamma, window=args.window, sink=args.sink, scaling=d ** -0.5)
+    # one workspace, reused across steps (the kernels never allocate)
+    ws = ops.prefill_workspace(U, G, 1, N, d, gamma=args.gamma, device=dev)
+
+    def step(evs=None):
+        if evs is not None:
+            evs[0].record()
+        ops.prefill(q, k, v, **kw, workspace=ws, out=out, phases=PHASE_ROWS)
+        if evs is not None:
+            evs[1].record()
+        ops.prefill(q, k, v, **kw, workspace=ws, out=out, phases=PHASE_WINDOW)
+        if evs is not None:
+            evs[2].record()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(physical_gpu(local_rank), enabled=not args.no_clocks) as clk:
+        torch.cuda.synchronize()
+        t_start.record()
+        for i in range(args.steps):
+            step(evs[i])
+        t_end.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_total = t_start.elapsed_time(t_end)
+    ms_rows = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
+    ms_win = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
+    if world > 1:
+        t = torch.tensor([ms_total, ms_rows, ms_win], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total, ms_rows, ms_win = t.tolist()
+    ms_step = ms_total / args.steps
+    tokens_per_step_job = N * n_seqs
+    value = tokens_per_step_job / (ms_step / 1000.0)
+
+    # roofline of the prefill kernel (both launches are the same kernel function)
+    flops_unit, flops_win_unit, flops_rows_unit = analytic_flops(G, d, N, args.window, args.sink, args.gamma)
+    flops_rank = flops_unit * U
+    peaks, peak_kind = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    ms_kernels = ms_rows + ms_win
+    achieved = flops_rank / (ms_kernels / 1000.0) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "prefill_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            tj = json.load(f)
+        if tj.get("seq") == N and tj.get("gamma") == args.gamma:
+            traffic = tj.get("bytes_per_step")
+
+    # e2e through the plug-in with pinned host buffers (rank-local units)
+    e2e = None
+    if not args.no_e2e:
+        from delta_attention_b200.attention import DeltaAttention
+        from delta_attention_b200.config import Config
+
+        class _ModelCfg:
+            pass
+
+        mc = _ModelCfg()
+        c = Config(delta_lambda=args.gamma, sliding_window=args.window, sink=args.sink, mode="delta")
+        for f_ in ("mode", "delta_lambda", "sliding_window", "sink", "q_block", "log_drift", "stride_policy"):
+            setattr(mc, f_, getattr(c, f_))
+        mc.num_attention_heads, mc.num_key_value_heads, mc.head_dim = G, 1, d
+        plug = DeltaAttention(mc)
+        qh, kh, vh = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+        oh = torch.empty(U, N, G, d, dtype=torch.bfloat16).pin_memory()
+        qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+        def e2e_step():
+            qd.copy_(qh, non_blocking=True)
+            kd.copy_(kh, non_blocking=True)
+            vd.copy_(vh, non_blocking=True)
+            o, _ = plug.delta_forward(plug, qd, kd, vd, None, scaling=d ** -0.5)
+            oh.copy_(o, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        s1.record()
+        torch.cuda.synchronize()
+        ms_e2e = s0.elapsed_time(s1) / args.e2e_steps
+        if world > 1:
+            t = torch.tensor([ms_e2e], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_e2e = t.item()
+        e2e = {"value": tokens_per_step_job / (ms_e2e / 1000.0), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2) * world,
+               "d2h_bytes_per_step": int(oh.numel() * 2) * world, "ms_per_step": ms_e2e,
+               "path": "DeltaAttention.delta_forward (plug-in surface) with pinned host q/k/v and output"}
+        del qh, kh, vh, oh, qd, kd, vd
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        val, cores, desc = cpu_baseline(args, args.cpu_seconds)
+        cpu = {"value": val, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1)*0.5 q/k/v, RoPE theta 5e5 on q/k)",
+            "config": workload_config(args, world),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
+                         "kernel": "dta::prefill_kernel<128> (rows launch + windowed launch)",
+                         "flops_per_step": flops_rank,
+                         "frac_of_sustained": achieved / float(peaks.get("bf16_tflops_sustained", 1400.0))},
+            "launches": {
+                "rows": {"ms": ms_rows, "tflops": flops_rows_unit * U / (ms_rows / 1000.0) / 1e12},
+                "window": {"ms": ms_win, "tflops": flops_win_unit * U / (ms_win / 1000.0) / 1e12},
+            },
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and world == 1 and args.gpus > 1:
+        print(json.dumps({"error": f"--gpus {args.gpus} needs torchrun with {args.gpus} processes"}), flush=True)
+        return 2
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -64,8 +64,13 @@ class PrefillArgs(ctypes.Structure):
         ("gamma", c_i32), ("window", c_i32), ("sink", c_i32), ("q_block", c_i32), ("mode", c_i32),
         ("anchors", c_vp), ("n_anchors", c_i32), ("s_p", c_i32),
         ("anchor_delta", c_vp),
+        ("phases", c_i32),
         ("workspace", c_vp), ("workspace_bytes", ctypes.c_size_t),
     ]
+
+
+PHASE_ROWS = 1
+PHASE_WINDOW = 2
 
 
 class RowsArgs(ctypes.Structure):

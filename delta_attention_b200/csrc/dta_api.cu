@@ -170,6 +170,8 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
     return DTA_ERR_STRIDE;
   if (!a->workspace || a->workspace_bytes < L.ws_bytes || !aligned16(a->workspace)) return DTA_ERR_WORKSPACE;
   if (a->anchor_delta && (a->mode != DTA_MODE_DELTA || !aligned16(a->anchor_delta))) return DTA_ERR_INVALID_ARG;
+  if (a->phases < 0 || a->phases > (DTA_PHASE_ROWS | DTA_PHASE_WINDOW)) return DTA_ERR_INVALID_ARG;
+  const int phases = a->phases ? a->phases : (DTA_PHASE_ROWS | DTA_PHASE_WINDOW);
   int sms = 0;
   if ((st = check_device(&sms)) != DTA_OK) return st;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
@@ -205,7 +207,7 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   if (e != cudaSuccess) return fail_cuda(e);
 
   // launch 1: dense rows (anchors + tail) and sparse anchor rows
-  if (a->mode != DTA_MODE_SPARSE_ONLY && L.n_sel > 0) {
+  if ((phases & DTA_PHASE_ROWS) && a->mode != DTA_MODE_SPARSE_ONLY && L.n_sel > 0) {
     dta::PrefillParams r = p;
     r.launch = dta::LAUNCH_ROWS;
     r.direct_from = (a->mode == DTA_MODE_DELTA) ? L.n_anchor : 0;
@@ -216,7 +218,7 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
     if ((e = dta::launch_prefill(r, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
   }
   // launch 2: windowed rows [0, row_end) with the fused delta epilogue
-  {
+  if (phases & DTA_PHASE_WINDOW) {
     dta::PrefillParams w = p;
     w.launch = dta::LAUNCH_WINDOW;
     w.row_end = (a->mode == DTA_MODE_SPARSE_ONLY) ? S : L.s_p;
@@ -227,7 +229,7 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
       if ((e = dta::launch_prefill(w, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
     }
   }
-  if (a->anchor_delta && L.buf_bytes) {
+  if ((phases & DTA_PHASE_ROWS) && a->anchor_delta && L.buf_bytes) {
     const long long n = (long long)B * L.n_anchor * H * d;
     if ((e = dta::launch_anchor_delta(p.dense_buf, p.sparse_buf, a->anchor_delta, n, stream)) != cudaSuccess)
       return fail_cuda(e);

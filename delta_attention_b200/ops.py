@@ -56,7 +56,8 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
 def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, window: int, sink: int,
             scaling: Optional[float] = None, mode: str = "delta", q_block: int = 64,
             anchors: Optional[torch.Tensor] = None, s_p: Optional[int] = None,
-            return_anchor_delta: bool = False, workspace: Optional[torch.Tensor] = None):
+            return_anchor_delta: bool = False, workspace: Optional[torch.Tensor] = None,
+            phases: int = 0, out: Optional[torch.Tensor] = None):
     """Delta-attention prefill of one layer.
 
     q [b, H, s, d], k/v [b, Hkv, s, d] (post-RoPE; any strides with d
@@ -75,7 +76,8 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
         scaling = d ** -0.5
     if mode not in _lib.MODES:
         raise ValueError(f"unknown mode {mode!r}")
-    out = torch.empty(b, s, H, d, dtype=torch.bfloat16, device=q.device)
+    if out is None:
+        out = torch.empty(b, s, H, d, dtype=torch.bfloat16, device=q.device)
     a = PrefillArgs()
     a.abi_version = ABI_VERSION
     a.batch, a.n_heads, a.n_kv_heads, a.seq_len, a.head_dim = b, H, Hkv, s, d
@@ -89,6 +91,7 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
     a.scaling = float(scaling)
     a.gamma, a.window, a.sink, a.q_block = int(gamma), int(window), int(sink), int(q_block)
     a.mode = _lib.MODES[mode]
+    a.phases = int(phases)
     anc = None
     if anchors is not None:
         anc = anchors.to(device=q.device, dtype=torch.int32).contiguous()
@@ -116,6 +119,39 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
     if odt != torch.bfloat16:
         out = out.to(odt)
     return (out, delta) if return_anchor_delta else out
+
+
+def prefill_workspace(batch: int, n_heads: int, n_kv_heads: int, seq_len: int, head_dim: int, *, gamma: int,
+                      mode: str = "delta", n_anchors: Optional[int] = None, s_p: Optional[int] = None,
+                      device=None) -> torch.Tensor:
+    """A device workspace of the size ``dta_prefill_workspace_size`` reports, for
+    callers that keep one workspace across calls."""
+    a = PrefillArgs()
+    a.abi_version = ABI_VERSION
+    a.batch, a.n_heads, a.n_kv_heads, a.seq_len, a.head_dim = batch, n_heads, n_kv_heads, seq_len, head_dim
+    a.gamma, a.window, a.sink, a.q_block, a.mode = int(gamma), 0, 0, 64, _lib.MODES[mode]
+    if n_anchors is not None:
+        a.anchors, a.n_anchors, a.s_p = 16, int(n_anchors), int(s_p)
+    nbytes = lib().dta_prefill_workspace_size(ctypes.byref(a))
+    if nbytes == 0:
+        raise ValueError("invalid prefill arguments for a workspace")
+    return _workspace(nbytes, device)
+
+
+def anchor_deltas(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rows: torch.Tensor, *, window: int,
+                  sink: int, scaling: Optional[float] = None, q_block: int = 64) -> torch.Tensor:
+    """dense - sparse (fp32) at the given sorted query rows, [b, n, H, d].
+
+    Runs only the row launch of the prefill (dense and sparse attention of the
+    listed rows); used by the adaptive stride planner."""
+    s = q.shape[2]
+    rows = rows.to(device=q.device, dtype=torch.int32)
+    # no tail rows (s_p == s) and no windowed launch: `out` is never written
+    dummy = torch.empty(16, dtype=torch.bfloat16, device=q.device)
+    _, delta = prefill(q, k, v, gamma=1, window=window, sink=sink, scaling=scaling, mode="delta",
+                       q_block=q_block, anchors=rows, s_p=s, return_anchor_delta=True,
+                       phases=_lib.PHASE_ROWS, out=dummy)
+    return delta
 
 
 def rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_rows: torch.Tensor, kv_limit: torch.Tensor,

@@ -90,9 +90,17 @@ typedef struct dta_prefill_args {
   int32_t s_p;            /* first dense-tail row (when anchors != NULL) */
   float* anchor_delta;    /* optional out [batch, n_anchor, n_heads, head_dim] fp32:
                              dense - sparse at every anchor (drift telemetry) */
+  int32_t phases;         /* 0 = whole prefill; otherwise a mask of DTA_PHASE_* */
   void* workspace;
   size_t workspace_bytes;
 } dta_prefill_args;
+
+/* Phases of dta_prefill.  ROWS: dense rows (anchors + tail) and sparse anchor
+ * rows, written to the workspace (and anchor_delta when given).  WINDOW: the
+ * windowed rows with the fused delta epilogue; it reads what a ROWS call with
+ * identical arguments left in the same workspace. */
+#define DTA_PHASE_ROWS 1
+#define DTA_PHASE_WINDOW 2
 
 /* Bytes of device workspace dta_prefill needs for these arguments. */
 DTA_API size_t dta_prefill_workspace_size(const dta_prefill_args* args);
