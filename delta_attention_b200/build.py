@@ -63,7 +63,7 @@ def build(force: bool = False, verbose: bool = False, extra=None) -> str:
         subprocess.run(cmd, check=True)
         objs.append(obj)
     tmp = LIB + ".tmp"
-    subprocess.run([nvcc(), "-shared", "-o", tmp] + objs + ARCH + ["-lcudart"], check=True)
+    subprocess.run([nvcc(), "-shared", "-o", tmp] + objs + ARCH + ["--cudart", "static"], check=True)
     os.replace(tmp, LIB)
     return LIB
 
