@@ -29,6 +29,7 @@ STATUS_NAMES = {
     8: "DTA_ERR_CUDA",
     9: "DTA_ERR_UNSUPPORTED_DEVICE",
     10: "DTA_ERR_KERNEL_TIMEOUT",
+    11: "DTA_ERR_SCRATCH_LIMIT",
 }
 
 MODES = {"delta": 0, "recompute": 1, "sparse-only": 2}
@@ -41,6 +42,7 @@ EXPORTED = (
     "dta_rows",
     "dta_decode_workspace_size",
     "dta_decode",
+    "dta_decode_noalloc",
     "dta_abi_version",
     "dta_status_string",
     "dta_last_cuda_error",
@@ -141,6 +143,8 @@ def lib() -> ctypes.CDLL:
         L.dta_decode_workspace_size.restype = ctypes.c_size_t
         L.dta_decode.argtypes = [ctypes.POINTER(DecodeArgs), c_vp]
         L.dta_decode.restype = ctypes.c_int
+        L.dta_decode_noalloc.argtypes = [ctypes.POINTER(DecodeArgs), c_vp]
+        L.dta_decode_noalloc.restype = ctypes.c_int
         L.dta_abi_version.argtypes = []
         L.dta_abi_version.restype = ctypes.c_int
         L.dta_status_string.argtypes = [ctypes.c_int]

@@ -50,7 +50,8 @@ typedef enum dta_status {
   DTA_ERR_WORKSPACE = 7,        /* workspace missing or smaller than *_workspace_size */
   DTA_ERR_CUDA = 8,             /* a CUDA runtime call failed (see dta_last_cuda_error) */
   DTA_ERR_UNSUPPORTED_DEVICE = 9, /* current device is not sm_100 */
-  DTA_ERR_KERNEL_TIMEOUT = 10   /* a kernel gave up on a bounded wait (dta_check_workspace) */
+  DTA_ERR_KERNEL_TIMEOUT = 10,  /* a kernel gave up on a bounded wait (dta_check_workspace) */
+  DTA_ERR_SCRATCH_LIMIT = 11    /* dta_decode_noalloc: request needs more scratch than its static array */
 } dta_status;
 
 typedef enum dta_mode {
@@ -154,6 +155,30 @@ typedef struct dta_decode_args {
 } dta_decode_args;
 DTA_API size_t dta_decode_workspace_size(const dta_decode_args* args);
 DTA_API int dta_decode(const dta_decode_args* args, void* stream);
+
+/* dta_decode for callers that cannot allocate device memory.  No counterpart in
+ * the reference (it is an addition of this library).
+ *
+ * Some callers cannot call cudaMalloc where they decode: a serving engine that
+ * has handed (nearly) all HBM to its own KV-cache and weight arenas, so a new
+ * allocation would fail or bypass the engine's accounting; a program in another
+ * language that binds only this C ABI and owns no device allocator; a
+ * latency-critical loop in which cudaMalloc/cudaFree would synchronize the device.
+ * This entry point ignores args->workspace/workspace_bytes and keeps the split-K
+ * partials in a static device array of DTA_DECODE_NOALLOC_SCRATCH_BYTES, which
+ * every GPU that loads this library holds until the process exits.
+ * - The first call on each device looks up that array's device address (with
+ *   that device current) and caches it; make that first call before any stream
+ *   capture begins.
+ * - A request whose dta_decode_workspace_size exceeds the array is rejected with
+ *   DTA_ERR_SCRATCH_LIMIT before anything is launched.
+ * - It allocates nothing.  All calls on a device share the one array, which keeps
+ *   the last call's contents; nothing in it needs to start at zero (every entry a
+ *   call reads was written earlier by the same call).  Calls whose kernels may
+ *   overlap on the GPU (different streams, or different host threads) race on the
+ *   array: order them on one stream. */
+#define DTA_DECODE_NOALLOC_SCRATCH_BYTES (32u << 20)
+DTA_API int dta_decode_noalloc(const dta_decode_args* args, void* stream);
 
 /* Host-side helpers. */
 DTA_API int dta_abi_version(void);
