@@ -179,7 +179,7 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   dta::PrefillParams p;
   memset(&p, 0, sizeof(p));
   const int B = a->batch, H = a->n_heads, Hkv = a->n_kv_heads, S = a->seq_len, d = a->head_dim;
-  const int G = H / Hkv, R = 128 / G;
+  const int G = H / Hkv, R = 128 / G, JR = dta::PREFILL_NQ * R;
   p.q = reinterpret_cast<const __nv_bfloat16*>(a->q);
   p.q_sb = a->q_stride_b; p.q_sh = a->q_stride_h; p.q_ss = a->q_stride_s;
   p.B = B; p.H = H; p.Hkv = Hkv; p.G = G; p.R = R;
@@ -211,8 +211,8 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
     dta::PrefillParams r = p;
     r.launch = dta::LAUNCH_ROWS;
     r.direct_from = (a->mode == DTA_MODE_DELTA) ? L.n_anchor : 0;
-    r.n_dense_tiles = (L.n_sel + R - 1) / R;
-    r.n_sparse_tiles = (a->mode == DTA_MODE_DELTA) ? (L.n_anchor + R - 1) / R : 0;
+    r.n_dense_tiles = (L.n_sel + JR - 1) / JR;
+    r.n_sparse_tiles = (a->mode == DTA_MODE_DELTA) ? (L.n_anchor + JR - 1) / JR : 0;
     r.n_jobs = (r.n_dense_tiles + r.n_sparse_tiles) * B * Hkv;
     const int grid = r.n_jobs < sms ? r.n_jobs : sms;
     if ((e = dta::launch_prefill(r, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
@@ -222,7 +222,7 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
     dta::PrefillParams w = p;
     w.launch = dta::LAUNCH_WINDOW;
     w.row_end = (a->mode == DTA_MODE_SPARSE_ONLY) ? S : L.s_p;
-    w.n_window_tiles = (w.row_end + R - 1) / R;
+    w.n_window_tiles = (w.row_end + JR - 1) / JR;
     w.n_jobs = w.n_window_tiles * B * Hkv;
     if (w.n_jobs > 0) {
       const int grid = w.n_jobs < sms ? w.n_jobs : sms;
@@ -261,7 +261,8 @@ int dta_rows(const dta_rows_args* a, void* stream_) {
   int sms = 0, st;
   if ((st = check_device(&sms)) != DTA_OK) return st;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  const int B = a->batch, H = a->n_heads, Hkv = a->n_kv_heads, d = a->head_dim, R = 128 / G;
+  const int B = a->batch, H = a->n_heads, Hkv = a->n_kv_heads, d = a->head_dim, R = 128 / G,
+            JR = dta::PREFILL_NQ * R;
   dta::PrefillParams p;
   memset(&p, 0, sizeof(p));
   p.q = reinterpret_cast<const __nv_bfloat16*>(a->q);
@@ -281,7 +282,7 @@ int dta_rows(const dta_rows_args* a, void* stream_) {
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
   p.counter = reinterpret_cast<int*>(ws);
   p.error = reinterpret_cast<int*>(ws) + 1;
-  p.n_dense_tiles = (a->n_rows + R - 1) / R;
+  p.n_dense_tiles = (a->n_rows + JR - 1) / JR;
   p.n_jobs = p.n_dense_tiles * B * Hkv;
   if ((st = encode_4d(&p.tm_k, a->k, d, a->kv_len, Hkv, B, a->k_stride_s, a->k_stride_h, a->k_stride_b, 128, 1)) !=
       DTA_OK)

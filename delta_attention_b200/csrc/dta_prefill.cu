@@ -15,13 +15,19 @@
 //                     out = sparse + (dense[a] - sparse[a]) for the owning anchor
 //                     a.  The sparse output never goes to HBM.
 //
-// One CTA = 128 query rows (R rows x G heads of one KV group, R = 128 / G, so
-// the whole GQA group shares every K/V tile) against 128-key tiles:
-//   warp 0      : producer (job fetch, Q by TMA or cp.async gather, K/V by TMA)
+// A job is two 128-row query tiles ("A" and "B"); a tile is R rows x G heads of
+// one KV group (R = 128 / G), so the whole GQA group shares every K/V tile.
+// Three warpgroups (384 threads; every thread stays within the 168-register
+// launch budget, so no register re-split is needed):
+//   warp 0      : producer (job fetch, Q by TMA or cp.async gather, K and V by TMA)
 //   warp 1      : TMEM owner; lane 0 issues every tcgen05.mma and commit
-//   warps 2..5  : softmax + epilogue, one thread per query row (TMEM lane)
-// TMEM: S double buffer (2 x 128 columns fp32, P aliased as packed bf16 in the
-// first 64 columns of its S buffer), O accumulator (head_dim columns).
+//   warps 2, 3  : idle
+//   warps 4..7  : softmax + epilogue of tile A, one thread per row (TMEM lane)
+//   warps 8..11 : softmax + epilogue of tile B
+// MMA issue order per key tile i:  PV_A(i), S_A(i+1), PV_B(i), S_B(i+1), so the
+// softmax of one tile overlaps the matrix products of the other.
+// TMEM: S_A, S_B (128 fp32 columns each; P is written back over S as packed
+// bf16 and read by the TS-form MMA), O_A, O_B (head_dim columns each).
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -36,8 +42,16 @@ namespace dta {
 
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 128 + PREFILL_NQ * 128;
+// Register split: launched at 168 per thread (384 x 168 = 64512), the control
+// warpgroup drops to 56 and the softmax warpgroups rise to 224:
+// 128 * 56 + 256 * 224 = 64512.
+constexpr int REGS_CONTROL = 104;
+constexpr int REGS_SOFTMAX = 200;
+static_assert(128 * REGS_CONTROL + PREFILL_NQ * 128 * REGS_SOFTMAX <= NUM_THREADS * 168, "register split");
 constexpr int CTRL_BYTES = 1024;
+constexpr int Q_SLOTS = 3;  // rotating Q tile slots: the next job's Q loads overlap this job
+constexpr int NQ = PREFILL_NQ;
 
 template <int HD>
 struct Geo {
@@ -46,19 +60,20 @@ struct Geo {
   static constexpr int TILE_BYTES = REGIONS * REGION_BYTES;  // one 128 x HD bf16 tile
   static constexpr int KV_STAGES = (HD == 128) ? 2 : 4;
   static constexpr int Q_OFF = CTRL_BYTES;
-  static constexpr int KV_OFF = Q_OFF + 2 * TILE_BYTES;
-  static constexpr int SMEM_BYTES = KV_OFF + KV_STAGES * 2 * TILE_BYTES + 1024;  // + alignment slack
+  static constexpr int K_OFF = Q_OFF + Q_SLOTS * TILE_BYTES;
+  static constexpr int V_OFF = K_OFF + KV_STAGES * TILE_BYTES;
+  static constexpr int SMEM_BYTES = V_OFF + KV_STAGES * TILE_BYTES + 1024;  // + alignment slack
   static constexpr int TMEM_COLS = 512;
-  static constexpr int O_COL = 256;
+  static constexpr int S_COL = 0;    // S of tile q at q * 128
+  static constexpr int O_COL = 256;  // O of tile q at 256 + q * 128
 };
 
-// control block layout (byte offsets inside the 1024-byte control area)
 struct Ctrl {
   uint64_t job_full[2], job_empty[2];
-  uint64_t q_full[2], q_empty[2];
-  uint64_t k_full[4], v_full[4], kv_empty[4];
-  uint64_t s_full[2], p_full[2];
-  uint64_t o_full, o_empty, drain;
+  uint64_t q_full[Q_SLOTS], q_empty[Q_SLOTS];
+  uint64_t k_full[4], k_empty[4], v_full[4], v_empty[4];
+  uint64_t s_full[NQ], p_full[NQ], o_full[NQ], o_empty[NQ];
+  uint64_t drain;
   int job[2][8];
   uint32_t tmem_base;
   int abort_flag;
@@ -68,11 +83,11 @@ static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block too large");
 enum JobKind : int { JOB_END = -1, JOB_WINDOW = 0, JOB_DENSE_ROWS = 1, JOB_SPARSE_ROWS = 2 };
 
 struct Job {
-  int kind, b, g, start, count, qmin, qmax, pad;
+  int kind, b, g, start, count;
 };
 
 // ---------------------------------------------------------------------------
-// row lists and job decoding (identical in every role)
+// row lists, jobs and key-tile plans (identical in every role)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int list_q_row(const PrefillParams& p, int i) {
   if (p.q_rows) return p.q_rows[i];
@@ -86,10 +101,10 @@ __device__ __forceinline__ int list_kv_limit(const PrefillParams& p, int i) {
 
 __device__ Job decode_job(const PrefillParams& p, int j) {
   Job J;
-  J.pad = 0;
+  const int JR = NQ * p.R;  // rows per job
   if (j >= p.n_jobs) {
     J.kind = JOB_END;
-    J.b = J.g = J.start = J.count = J.qmin = J.qmax = 0;
+    J.b = J.g = J.start = J.count = 0;
     return J;
   }
   if (p.launch == LAUNCH_WINDOW) {
@@ -98,10 +113,8 @@ __device__ Job decode_job(const PrefillParams& p, int j) {
     J.kind = JOB_WINDOW;
     J.b = bg / p.Hkv;
     J.g = bg - J.b * p.Hkv;
-    J.start = t * p.R;
-    J.count = min(p.R, p.row_end - J.start);
-    J.qmin = J.start;
-    J.qmax = J.start + J.count - 1;
+    J.start = t * JR;
+    J.count = min(JR, p.row_end - J.start);
     return J;
   }
   const int BG = p.B * p.Hkv;
@@ -111,47 +124,81 @@ __device__ Job decode_job(const PrefillParams& p, int j) {
   if (rank < p.n_dense_tiles) {
     const int tile = p.n_dense_tiles - 1 - rank;  // longest (latest rows) first
     J.kind = JOB_DENSE_ROWS;
-    J.start = tile * p.R;
-    J.count = min(p.R, p.n_sel - J.start);
+    J.start = tile * JR;
+    J.count = min(JR, p.n_sel - J.start);
   } else {
     const int tile = rank - p.n_dense_tiles;
     J.kind = JOB_SPARSE_ROWS;
-    J.start = tile * p.R;
-    J.count = min(p.R, p.n_anchor - J.start);
+    J.start = tile * JR;
+    J.count = min(JR, p.n_anchor - J.start);
   }
-  J.qmin = list_kv_limit(p, J.start);
-  J.qmax = list_kv_limit(p, J.start + J.count - 1);
   return J;
 }
 
-struct Plan {
-  int n0, n_tiles, sink_end, lo_min, lo_max;
-};
+// position (key limit) of job-local row r (< J.count)
+__device__ __forceinline__ int job_row_pos(const PrefillParams& p, const Job& J, int r) {
+  if (J.kind == JOB_WINDOW) return J.start + r;
+  return list_kv_limit(p, J.start + r);
+}
 
 __device__ __forceinline__ int block_window_lo(const PrefillParams& p, int t) {
   const int bl = (t / p.qblock) * p.qblock + p.qblock - 1;
   return max(0, bl - p.window + 1);
 }
 
-__device__ __forceinline__ Plan make_plan(const PrefillParams& p, const Job& J) {
+// Key tiles of a job: sink segment [0, sink_end) then window segment
+// [lo_min, qmax]; dense jobs have only [0, qmax].  Query tile q takes the
+// prefix of tiles whose first key is <= the tile's last row.
+struct Plan {
+  int n0, n_tiles, sink_end, lo_min, qmax;
+  int qmin_t[NQ], qmax_t[NQ], lo_max_t[NQ], tiles_t[NQ];
+};
+
+__device__ __forceinline__ int tile_key_start(const Plan& P, int i) {
+  return i < P.n0 ? i * BN : P.lo_min + (i - P.n0) * BN;
+}
+
+__device__ Plan make_plan(const PrefillParams& p, const Job& J) {
   Plan P;
-  if (J.kind == JOB_DENSE_ROWS) {
+  const bool dense = (J.kind == JOB_DENSE_ROWS);
+  int first = -1;
+  P.qmax = 0;
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    const int r0 = q * p.R;
+    const int r1 = min(J.count, (q + 1) * p.R) - 1;
+    if (r1 < r0) {
+      P.qmin_t[q] = 0;
+      P.qmax_t[q] = -1;
+      P.lo_max_t[q] = 0;
+      continue;
+    }
+    P.qmin_t[q] = job_row_pos(p, J, r0);
+    P.qmax_t[q] = job_row_pos(p, J, r1);
+    P.lo_max_t[q] = dense ? 0 : block_window_lo(p, P.qmax_t[q]);
+    if (first < 0) first = P.qmin_t[q];
+    P.qmax = max(P.qmax, P.qmax_t[q]);
+  }
+  if (dense) {
     P.n0 = 0;
     P.sink_end = 0;
     P.lo_min = 0;
-    P.lo_max = 0;
-    P.n_tiles = (J.qmax + BN) / BN;
+    P.n_tiles = P.qmax / BN + 1;
   } else {
-    P.lo_min = block_window_lo(p, J.qmin);
-    P.lo_max = block_window_lo(p, J.qmax);
+    P.lo_min = block_window_lo(p, first);
     P.sink_end = min(p.sink, P.lo_min);
     P.n0 = (P.sink_end + BN - 1) / BN;
-    P.n_tiles = P.n0 + (J.qmax - P.lo_min + BN) / BN;
+    P.n_tiles = P.n0 + (P.qmax - P.lo_min) / BN + 1;
+  }
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    const int m = P.qmax_t[q];
+    if (m < 0) P.tiles_t[q] = 0;
+    else if (dense) P.tiles_t[q] = m / BN + 1;
+    else if (m >= P.lo_min) P.tiles_t[q] = P.n0 + (m - P.lo_min) / BN + 1;
+    else P.tiles_t[q] = min(P.n0, m / BN + 1);
   }
   return P;
-}
-__device__ __forceinline__ int tile_key_start(const Plan& P, int i) {
-  return i < P.n0 ? i * BN : P.lo_min + (i - P.n0) * BN;
 }
 
 // ---------------------------------------------------------------------------
@@ -168,7 +215,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   const uint32_t ctrl_u32 = base_u32;
 #define BAR(field) (ctrl_u32 + (uint32_t)offsetof(Ctrl, field))
   const uint32_t q_u32 = base_u32 + G::Q_OFF;
-  const uint32_t kv_u32 = base_u32 + G::KV_OFF;
+  const uint32_t k_u32 = base_u32 + G::K_OFF;
+  const uint32_t v_u32 = base_u32 + G::V_OFF;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -178,19 +226,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(BAR(job_full[0]) + 8 * i, 1);
-      mbar_init(BAR(job_empty[0]) + 8 * i, 5);  // MMA thread + 4 softmax warps
+      mbar_init(BAR(job_empty[0]) + 8 * i, 1 + 4 * NQ);  // MMA thread + every softmax warp
+    }
+    for (int i = 0; i < Q_SLOTS; ++i) {
       mbar_init(BAR(q_full[0]) + 8 * i, 1);
       mbar_init(BAR(q_empty[0]) + 8 * i, 1);
-      mbar_init(BAR(s_full[0]) + 8 * i, 1);
-      mbar_init(BAR(p_full[0]) + 8 * i, 4);
     }
     for (int i = 0; i < G::KV_STAGES; ++i) {
       mbar_init(BAR(k_full[0]) + 8 * i, 1);
+      mbar_init(BAR(k_empty[0]) + 8 * i, 1);
       mbar_init(BAR(v_full[0]) + 8 * i, 1);
-      mbar_init(BAR(kv_empty[0]) + 8 * i, 1);
+      mbar_init(BAR(v_empty[0]) + 8 * i, 1);
     }
-    mbar_init(BAR(o_full), 1);
-    mbar_init(BAR(o_empty), 4);
+    for (int q = 0; q < NQ; ++q) {
+      mbar_init(BAR(s_full[0]) + 8 * q, 1);
+      mbar_init(BAR(p_full[0]) + 8 * q, 4);
+      mbar_init(BAR(o_full[0]) + 8 * q, 1);
+      mbar_init(BAR(o_empty[0]) + 8 * q, 4);
+    }
     mbar_init(BAR(drain), 1);
     ctrl->abort_flag = 0;
     mbar_init_fence();
@@ -212,11 +265,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   tc_fence_after();
   const uint32_t tmem = ctrl->tmem_base;
 
+  if (warp < 4) {
   if (warp == 0) {
     // ======================= producer =======================
-    int n = 0;  // global K/V tile counter
-    int issued_last_stage_n = -1;
-    for (int it = 0;; ++it) {
+    int n = 0;      // K/V tiles issued so far (ring position)
+    int qload = 0;  // Q tiles loaded so far (slot = qload % Q_SLOTS)
+    bool ok = true;
+    for (int it = 0; ok; ++it) {
       const int slot = it & 1;
       int j;
       if (p.launch == LAUNCH_WINDOW) {
@@ -226,82 +281,94 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         if (lane == 0) jj = atomicAdd(p.counter, 1);
         j = __shfl_sync(0xffffffffu, jj, 0);
       }
-      if (!mbar_wait_warp(BAR(job_empty[0]) + 8 * slot, ((it >> 1) & 1) ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER))
+      if (!mbar_wait_warp(BAR(job_empty[0]) + 8 * slot, ((it >> 1) & 1) ^ 1, abort_flag, err,
+                          KERR_TIMEOUT_PRODUCER))
         break;
       const Job J = decode_job(p, j);
       if (lane == 0) {
         int* dst = ctrl->job[slot];
-        dst[0] = J.kind; dst[1] = J.b; dst[2] = J.g; dst[3] = J.start;
-        dst[4] = J.count; dst[5] = J.qmin; dst[6] = J.qmax; dst[7] = 0;
+        dst[0] = J.kind; dst[1] = J.b; dst[2] = J.g; dst[3] = J.start; dst[4] = J.count;
         mbar_arrive(BAR(job_full[0]) + 8 * slot);
       }
       if (J.kind == JOB_END) break;
-      // ---- Q tile (double-buffered across jobs) ----
-      const uint32_t qbuf = q_u32 + (uint32_t)(it & 1) * G::TILE_BYTES;
-      if (!mbar_wait_warp(BAR(q_empty[0]) + 8 * (it & 1), ((it >> 1) & 1) ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER))
-        break;
-      if (J.kind == JOB_WINDOW) {
-        if (lane == 0) {
-          mbar_arrive_expect_tx(BAR(q_full[0]) + 8 * (it & 1), G::TILE_BYTES);
-          for (int r = 0; r < G::REGIONS; ++r)
-            tma_load_4d(qbuf + r * G::REGION_BYTES, &p.tm_q, BAR(q_full[0]) + 8 * (it & 1), r * 64, J.start,
-                        J.g * p.G, J.b);
-        }
-      } else {
-        // gather 128 rows (R list rows x G heads) with cp.async into the
-        // 128-byte-swizzled K-major layout the MMA expects
-        constexpr int CH = HD / 8;  // 16-byte chunks per row
-        const __nv_bfloat16* qb = p.q + (long long)J.b * p.q_sb;
-        for (int c = lane; c < BM * CH; c += 32) {
-          const int m = c / CH, cc = c - (c / CH) * CH;
-          const int hh = m / p.R, rr = m - (m / p.R) * p.R;
-          const bool valid = rr < J.count;
-          const int row = valid ? list_q_row(p, J.start + rr) : 0;
-          const __nv_bfloat16* src =
-              qb + (long long)(J.g * p.G + hh) * p.q_sh + (long long)row * p.q_ss + cc * 8;
-          const int region = cc >> 3, cw = cc & 7;
-          const uint32_t dst = qbuf + region * G::REGION_BYTES + m * 128 + ((cw ^ (m & 7)) << 4);
-          cp_async_16(dst, src, valid ? 16u : 0u);
-        }
-        cp_async_wait_all();
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(BAR(q_full[0]) + 8 * (it & 1));
-      }
-      // ---- K/V tiles ----
       const Plan P = make_plan(p, J);
-      bool ok = true;
+      // ---- Q tiles ----
+      for (int q = 0; q < NQ; ++q) {
+        if (P.tiles_t[q] == 0) continue;
+        const int qs = qload % Q_SLOTS;
+        const uint32_t qbuf = q_u32 + (uint32_t)qs * G::TILE_BYTES;
+        if (!mbar_wait_warp(BAR(q_empty[0]) + 8 * qs, ((qload / Q_SLOTS) & 1) ^ 1, abort_flag, err,
+                            KERR_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        ++qload;
+        if (J.kind == JOB_WINDOW) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(BAR(q_full[0]) + 8 * qs, G::TILE_BYTES);
+            for (int r = 0; r < G::REGIONS; ++r)
+              tma_load_4d(qbuf + r * G::REGION_BYTES, &p.tm_q, BAR(q_full[0]) + 8 * qs, r * 64,
+                          J.start + q * p.R, J.g * p.G, J.b);
+          }
+        } else {
+          // gather R list rows x G heads with cp.async into the 128-byte-
+          // swizzled K-major layout the MMA expects
+          constexpr int CH = HD / 8;  // 16-byte chunks per row
+          const __nv_bfloat16* qb = p.q + (long long)J.b * p.q_sb;
+          for (int c = lane; c < BM * CH; c += 32) {
+            const int m = c / CH, cc = c - (c / CH) * CH;
+            const int hh = m / p.R, rr = m - (m / p.R) * p.R;
+            const int li = q * p.R + rr;
+            const bool valid = li < J.count;
+            const int row = valid ? list_q_row(p, J.start + li) : 0;
+            const __nv_bfloat16* src =
+                qb + (long long)(J.g * p.G + hh) * p.q_sh + (long long)row * p.q_ss + cc * 8;
+            const int region = cc >> 3, cw = cc & 7;
+            const uint32_t dst = qbuf + region * G::REGION_BYTES + m * 128 + ((cw ^ (m & 7)) << 4);
+            cp_async_16(dst, src, valid ? 16u : 0u);
+          }
+          cp_async_wait_all();
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(BAR(q_full[0]) + 8 * qs);
+        }
+      }
+      if (!ok) break;
+      // ---- K and V tiles ----
       for (int i = 0; i < P.n_tiles; ++i, ++n) {
         const int st = n % G::KV_STAGES;
         const uint32_t ph = (uint32_t)((n / G::KV_STAGES) & 1);
-        if (!mbar_wait_warp(BAR(kv_empty[0]) + 8 * st, ph ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER)) {
+        const int ks = tile_key_start(P, i);
+        if (!mbar_wait_warp(BAR(k_empty[0]) + 8 * st, ph ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
         }
         if (lane == 0) {
-          const int ks = tile_key_start(P, i);
-          const uint32_t kdst = kv_u32 + (uint32_t)st * 2 * G::TILE_BYTES;
-          const uint32_t vdst = kdst + G::TILE_BYTES;
+          const uint32_t kdst = k_u32 + (uint32_t)st * G::TILE_BYTES;
           mbar_arrive_expect_tx(BAR(k_full[0]) + 8 * st, G::TILE_BYTES);
           for (int r = 0; r < G::REGIONS; ++r)
             tma_load_4d(kdst + r * G::REGION_BYTES, &p.tm_k, BAR(k_full[0]) + 8 * st, r * 64, ks, J.g, J.b);
+        }
+        if (!mbar_wait_warp(BAR(v_empty[0]) + 8 * st, ph ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const uint32_t vdst = v_u32 + (uint32_t)st * G::TILE_BYTES;
           mbar_arrive_expect_tx(BAR(v_full[0]) + 8 * st, G::TILE_BYTES);
           for (int r = 0; r < G::REGIONS; ++r)
             tma_load_4d(vdst + r * G::REGION_BYTES, &p.tm_v, BAR(v_full[0]) + 8 * st, r * 64, ks, J.g, J.b);
         }
-        issued_last_stage_n = n;
       }
-      if (!ok) break;
     }
     // On abort, let in-flight TMA loads land before the CTA can exit.
     if (*abort_flag && lane == 0) {
-      for (int m = max(0, issued_last_stage_n - G::KV_STAGES + 1); m <= issued_last_stage_n; ++m) {
+      for (int m = max(0, n - G::KV_STAGES); m < n; ++m) {
         const int st = m % G::KV_STAGES;
         const uint32_t ph = (uint32_t)((m / G::KV_STAGES) & 1);
-        volatile int never = 0;
-        long long t0 = clock64();
+        const long long t0 = clock64();
         while (!(mbar_try_wait(BAR(k_full[0]) + 8 * st, ph) && mbar_try_wait(BAR(v_full[0]) + 8 * st, ph))) {
-          if (clock64() - t0 > kWaitTimeoutCycles || never) break;
+          if (clock64() - t0 > kWaitTimeoutCycles) break;
         }
       }
     }
@@ -310,156 +377,172 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     if (lane == 0) {
       constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, BN, 0);
       constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, HD, 1);
-      const uint32_t tO = tmem + G::O_COL;
-      int n = 0;
-      bool have_pending = false, aborted = false;
-      int pend_n = 0, pend_stage = 0, pend_first = 0;
-      int jobs_pv = 0;  // number of jobs whose first PV has been issued
-
-      auto do_pv = [&](int m, int stage, int first) -> bool {
-        if (!mbar_wait(BAR(p_full[0]) + 8 * (m & 1), (m >> 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
-        if (first) {
-          if (jobs_pv > 0 &&
-              !mbar_wait(BAR(o_empty), (jobs_pv - 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
-            return false;
-          ++jobs_pv;
-        }
-        if (!mbar_wait(BAR(v_full[0]) + 8 * stage, (m / G::KV_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
-          return false;
-        tc_fence_after();
-        const uint32_t tP = tmem + (uint32_t)(m & 1) * 128;
-        const uint32_t vbase = kv_u32 + (uint32_t)stage * 2 * G::TILE_BYTES + G::TILE_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bdesc = smem_desc_sw128(vbase + kk * 2048, G::REGION_BYTES, 1024);
-          umma_ts(tO, tP + kk * 8, bdesc, IDESC_PV, (first && kk == 0) ? 0u : 1u);
-        }
-        umma_commit(BAR(kv_empty[0]) + 8 * stage);
-        umma_commit(BAR(o_full));
-        return true;
-      };
-
-      for (int it = 0;; ++it) {
+      int n = 0;                // K/V tiles consumed so far (ring position)
+      int qload = 0;            // Q tiles consumed so far (slot position)
+      int cnt_s[NQ] = {0, 0};   // S tiles issued per query tile (= PVs)
+      int jobs_t[NQ] = {0, 0};  // jobs in which query tile q was active
+      bool aborted = false;
+      for (int it = 0; !aborted; ++it) {
         const int slot = it & 1;
-        if (!mbar_wait(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) {
-          aborted = true;
-          break;
-        }
+        if (!mbar_wait(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) break;
         Job J;
         {
           const volatile int* src = ctrl->job[slot];
-          J.kind = src[0]; J.b = src[1]; J.g = src[2]; J.start = src[3];
-          J.count = src[4]; J.qmin = src[5]; J.qmax = src[6];
+          J.kind = src[0]; J.b = src[1]; J.g = src[2]; J.start = src[3]; J.count = src[4];
         }
         mbar_arrive(BAR(job_empty[0]) + 8 * slot);
         if (J.kind == JOB_END) break;
         const Plan P = make_plan(p, J);
-        const uint32_t qbuf = q_u32 + (uint32_t)(it & 1) * G::TILE_BYTES;
-        if (!mbar_wait(BAR(q_full[0]) + 8 * (it & 1), (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) {
-          aborted = true;
-          break;
-        }
-        for (int i = 0; i < P.n_tiles; ++i, ++n) {
-          const int st = n % G::KV_STAGES;
-          if (!mbar_wait(BAR(k_full[0]) + 8 * st, (n / G::KV_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) {
+        uint32_t qbuf[NQ];
+        int qslot[NQ];
+        for (int q = 0; q < NQ; ++q) {
+          qbuf[q] = 0;
+          qslot[q] = 0;
+          if (P.tiles_t[q] == 0) continue;
+          qslot[q] = qload % Q_SLOTS;
+          qbuf[q] = q_u32 + (uint32_t)qslot[q] * G::TILE_BYTES;
+          if (!mbar_wait(BAR(q_full[0]) + 8 * qslot[q], (qload / Q_SLOTS) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) {
             aborted = true;
             break;
           }
+          ++qload;
+        }
+        if (aborted) break;
+        const int n0 = n;  // ring position of this job's key tile 0
+        // the last query tile active at key tile i releases K_i / V_i
+        auto last_active = [&](int i) { return (i < P.tiles_t[NQ - 1]) ? NQ - 1 : 0; };
+        // S_q(i) = Q_q . K_i^T
+        auto issue_s = [&](int q, int i) -> bool {
+          const int m = n0 + i, st = m % G::KV_STAGES;
+          if (q == 0 || i >= P.tiles_t[0]) {  // first user of K_i waits for it
+            if (!mbar_wait(BAR(k_full[0]) + 8 * st, (m / G::KV_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+              return false;
+          }
           tc_fence_after();
-          const uint32_t tS = tmem + (uint32_t)(n & 1) * 128;
-          const uint32_t kbase = kv_u32 + (uint32_t)st * 2 * G::TILE_BYTES;
+          const uint32_t tS = tmem + G::S_COL + q * 128;
+          const uint32_t kbase = k_u32 + (uint32_t)st * G::TILE_BYTES;
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off = (kk >> 2) * G::REGION_BYTES + (kk & 3) * 32;
-            const uint64_t adesc = smem_desc_sw128(qbuf + off, 16, 1024);
-            const uint64_t bdesc = smem_desc_sw128(kbase + off, 16, 1024);
-            umma_ss(tS, adesc, bdesc, IDESC_QK, kk > 0 ? 1u : 0u);
+            umma_ss(tS, smem_desc_sw128(qbuf[q] + off, 16, 1024), smem_desc_sw128(kbase + off, 16, 1024), IDESC_QK,
+                    kk > 0 ? 1u : 0u);
           }
-          umma_commit(BAR(s_full[0]) + 8 * (n & 1));
-          if (i == P.n_tiles - 1) umma_commit(BAR(q_empty[0]) + 8 * (it & 1));
-          if (have_pending && !do_pv(pend_n, pend_stage, pend_first)) {
-            aborted = true;
-            break;
+          umma_commit(BAR(s_full[0]) + 8 * q);
+          ++cnt_s[q];
+          if (q == last_active(i)) umma_commit(BAR(k_empty[0]) + 8 * st);
+          if (i == P.tiles_t[q] - 1) umma_commit(BAR(q_empty[0]) + 8 * qslot[q]);
+          return true;
+        };
+        // O_q += P_q(i) . V_i   (S_q(i) is the last S issued for q at this point)
+        auto issue_pv = [&](int q, int i) -> bool {
+          const int m = n0 + i, st = m % G::KV_STAGES;
+          if (!mbar_wait(BAR(p_full[0]) + 8 * q, (cnt_s[q] - 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
+          if (i == 0 && jobs_t[q] > 0) {
+            if (!mbar_wait(BAR(o_empty[0]) + 8 * q, (jobs_t[q] - 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+              return false;
           }
-          have_pending = true;
-          pend_n = n;
-          pend_stage = st;
-          pend_first = (i == 0);
+          if (q == 0 || i >= P.tiles_t[0]) {  // first user of V_i waits for it
+            if (!mbar_wait(BAR(v_full[0]) + 8 * st, (m / G::KV_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+              return false;
+          }
+          tc_fence_after();
+          const uint32_t tP = tmem + G::S_COL + q * 128;
+          const uint32_t tO = tmem + G::O_COL + q * 128;
+          const uint32_t vbase = v_u32 + (uint32_t)st * G::TILE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk)
+            umma_ts(tO, tP + kk * 8, smem_desc_sw128(vbase + kk * 2048, G::REGION_BYTES, 1024), IDESC_PV,
+                    (i == 0 && kk == 0) ? 0u : 1u);
+          umma_commit(BAR(o_full[0]) + 8 * q);
+          if (q == last_active(i)) umma_commit(BAR(v_empty[0]) + 8 * st);
+          return true;
+        };
+        // prologue: S of key tile 0 for every active query tile
+        for (int q = 0; q < NQ && !aborted; ++q)
+          if (P.tiles_t[q] > 0 && !issue_s(q, 0)) aborted = true;
+        for (int i = 0; i < P.n_tiles && !aborted; ++i) {
+          for (int q = 0; q < NQ; ++q) {
+            if (i >= P.tiles_t[q]) continue;
+            if (!issue_pv(q, i)) {
+              aborted = true;
+              break;
+            }
+            if (i + 1 < P.tiles_t[q] && !issue_s(q, i + 1)) {
+              aborted = true;
+              break;
+            }
+          }
         }
         if (aborted) break;
+        for (int q = 0; q < NQ; ++q)
+          if (P.tiles_t[q] > 0) ++jobs_t[q];
+        n += P.n_tiles;
       }
-      if (!aborted && have_pending) do_pv(pend_n, pend_stage, pend_first);
       // drain: every issued tcgen05 op completes before TMEM is released
       umma_commit(BAR(drain));
-      {
-        long long t0 = clock64();
-        while (!mbar_try_wait(BAR(drain), 0)) {
-          if (clock64() - t0 > kWaitTimeoutCycles) {
-            atomicCAS(err, 0, KERR_TIMEOUT_DRAIN);
-            break;
-          }
+      const long long t0 = clock64();
+      while (!mbar_try_wait(BAR(drain), 0)) {
+        if (clock64() - t0 > kWaitTimeoutCycles) {
+          atomicCAS(err, 0, KERR_TIMEOUT_DRAIN);
+          break;
         }
       }
     }
+  }
   } else {
     // ======================= softmax + epilogue =======================
-    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
-    const int r = quarter * 32 + lane;       // query row of this thread inside the tile
+    const int q = (warp - 4) >> 2;        // query tile of this warpgroup
+    const int quarter = warp & 3;         // TMEM lane quarter this warp may access
+    const int r = quarter * 32 + lane;    // row of this thread inside its query tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int hh = r / p.R, rr = r - (r / p.R) * p.R;
+    const uint32_t tS = tmem + lane_off + G::S_COL + q * 128;
+    const uint32_t tO = tmem + lane_off + G::O_COL + q * 128;
     const float sl2 = p.scale_log2;
-    int n = 0;
+    int cnt = 0;  // S tiles consumed by this warpgroup (= PVs of its query tile)
     for (int it = 0;; ++it) {
       const int slot = it & 1;
       if (!mbar_wait_warp(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
       Job J;
       {
         const volatile int* src = ctrl->job[slot];
-        J.kind = src[0]; J.b = src[1]; J.g = src[2]; J.start = src[3];
-        J.count = src[4]; J.qmin = src[5]; J.qmax = src[6];
+        J.kind = src[0]; J.b = src[1]; J.g = src[2]; J.start = src[3]; J.count = src[4];
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(job_empty[0]) + 8 * slot);
       if (J.kind == JOB_END) break;
       const Plan P = make_plan(p, J);
-      const bool row_valid = rr < J.count;
-      int qpos;
-      if (J.kind == JOB_WINDOW) qpos = J.start + rr;
-      else qpos = row_valid ? list_kv_limit(p, J.start + rr) : J.qmax;
+      const int T = P.tiles_t[q];
+      if (T == 0) continue;  // this query tile is empty in this job
+      const int li = q * p.R + rr;  // job-local row
+      const bool row_valid = li < J.count;
+      const int qpos = row_valid ? job_row_pos(p, J, li) : P.qmax_t[q];
       const bool sparse_kind = (J.kind != JOB_DENSE_ROWS);
       const int lo_q = sparse_kind ? block_window_lo(p, qpos) : 0;
       const int sink_q = sparse_kind ? p.sink : 0x7fffffff;
+      const int qmin_t = P.qmin_t[q];
+      const int lo_max_t = P.lo_max_t[q];
 
       float m_run = -INFINITY, l_run = 0.f;
       bool aborted = false;
-      for (int i = 0; i < P.n_tiles; ++i, ++n) {
-        if (!mbar_wait_warp(BAR(s_full[0]) + 8 * (n & 1), (n >> 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
+      for (int i = 0; i < T; ++i, ++cnt) {
+        if (!mbar_wait_warp(BAR(s_full[0]) + 8 * q, cnt & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
           aborted = true;
           break;
         }
         tc_fence_after();
-        const uint32_t tS = tmem + lane_off + (uint32_t)(n & 1) * 128;
-        float s[BN];
-        {
-          uint32_t u[32];
-#pragma unroll
-          for (int c = 0; c < BN / 32; ++c) {
-            tmem_ld32(tS + c * 32, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(u[e]);
-          }
-        }
         const int ks = tile_key_start(P, i);
         const int seg_lo = (i < P.n0) ? 0 : P.lo_min;
-        const int seg_hi = (i < P.n0) ? P.sink_end : J.qmax + 1;  // exclusive
-        const bool full = (ks >= seg_lo) && (ks + BN <= seg_hi) && (ks + BN - 1 <= J.qmin) &&
-                          (!sparse_kind || ks + BN <= p.sink || ks >= P.lo_max);
-        float mt = -INFINITY;
-        if (full) {
+        const int seg_hi = (i < P.n0) ? P.sink_end : P.qmax + 1;  // exclusive
+        const bool full = (ks >= seg_lo) && (ks + BN <= seg_hi) && (ks + BN - 1 <= qmin_t) &&
+                          (!sparse_kind || ks + BN <= p.sink || ks >= lo_max_t);
+        // load the whole S row (4 x 32 columns) behind a single wait
+        float x[BN];
 #pragma unroll
-          for (int e = 0; e < BN; ++e) mt = fmaxf(mt, s[e]);
-        } else {
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32f(tS + c * 32, x + c * 32);
+        tmem_wait_ld();
+        if (!full) {
+          // column window of this row: valid iff A <= c <= Bq and not X <= c < Y
           const int A = seg_lo - ks;
           const int Bq = min(seg_hi - 1, qpos) - ks;
           const int X = sink_q - ks;
@@ -467,42 +550,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
 #pragma unroll
           for (int e = 0; e < BN; ++e) {
             const bool v = (e >= A) && (e <= Bq) && !((e >= X) && (e < Y));
-            s[e] = v ? s[e] : -INFINITY;
-            mt = fmaxf(mt, s[e]);
+            x[e] = v ? x[e] : -INFINITY;
           }
         }
+        float mt = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < BN; ++e) mt = fmaxf(mt, x[e]);
         mt *= sl2;  // scaled units (log2 domain); -inf stays -inf
-        if (i > 0) {
-          // PV of the previous tile must be complete before O is touched or P is released
-          if (!mbar_wait_warp(BAR(o_full), (n - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
-            aborted = true;
-            break;
-          }
-          tc_fence_after();
-          // rescale only on a large max increase; the TMEM round trip is
-          // warp-collective, so lanes that do not need it scale by 1
-          const bool need = mt > m_run + 8.0f;
-          if (__any_sync(0xffffffffu, need)) {
-            const float alpha = !need ? 1.f : ((m_run == -INFINITY) ? 0.f : fast_exp2(m_run - mt));
-            const uint32_t tO = tmem + lane_off + G::O_COL;
-            uint32_t u[32];
-#pragma unroll
-            for (int c = 0; c < HD / 32; ++c) {
-              tmem_ld32(tO + c * 32, u);
-              tmem_wait_ld();
-#pragma unroll
-              for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
-              tmem_st32(tO + c * 32, u);
-            }
-            if (need) {
-              l_run *= alpha;
-              m_run = mt;
-            }
-          }
-        } else {
-          m_run = mt;
-        }
-        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        // keep the running max unless it grows by more than 2^8 (exact: O and
+        // l always share the reference max; P stays <= 256)
+        const bool need = (i > 0) && (mt > m_run + 8.0f);
+        const float m_new = (i == 0 || need) ? mt : m_run;
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
         float lsum = 0.f;
         __syncwarp();  // converge before the warp-collective TMEM stores
 #pragma unroll
@@ -510,31 +569,51 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const float p0 = fast_exp2(fmaf(s[c * 32 + 2 * e], sl2, -m_use));
-            const float p1 = fast_exp2(fmaf(s[c * 32 + 2 * e + 1], sl2, -m_use));
+            const float p0 = fast_exp2(fmaf(x[c * 32 + 2 * e], sl2, -m_use));
+            const float p1 = fast_exp2(fmaf(x[c * 32 + 2 * e + 1], sl2, -m_use));
             lsum += p0 + p1;
             pk[e] = pack_bf16x2(p0, p1);
           }
           tmem_st16(tS + c * 16, pk);
         }
+        if (i > 0) {
+          // PV of the previous tile must be complete before O is rescaled or
+          // P is released to the next PV
+          if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, (cnt - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          // the TMEM round trip is warp-collective: lanes that keep their max scale by 1
+          if (__any_sync(0xffffffffu, need)) {
+            const float alpha = !need ? 1.f : ((m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new));
+#pragma unroll
+            for (int c = 0; c < HD / 32; ++c) {
+              float o[32];
+              tmem_ld32f(tO + c * 32, o);
+              tmem_wait_ld();
+              uint32_t u[32];
+#pragma unroll
+              for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(o[e] * alpha);
+              tmem_st32(tO + c * 32, u);
+            }
+            if (need) l_run *= alpha;
+          }
+        }
+        m_run = m_new;
         l_run += lsum;
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(BAR(p_full[0]) + 8 * (n & 1));
+        if (lane == 0) mbar_arrive(BAR(p_full[0]) + 8 * q);
       }
       if (aborted) break;
       // ---- epilogue: wait for the last PV, normalise, correct, store ----
-      if (!mbar_wait_warp(BAR(o_full), (n - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
+      if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, (cnt - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
       tc_fence_after();
       const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
       const int h = J.g * p.G + hh;
-      const uint32_t tO = tmem + lane_off + G::O_COL;
-      // destination of this row
-      // window: out[b, qpos, h, :] (bf16), rows < row_end, optionally + delta of owning anchor
-      // dense rows: list index < direct_from -> dense_buf fp32 ; else out[b, q_row, h, :] bf16
-      // sparse rows: sparse_buf fp32
-      const int li = J.start + rr;
+      const int gli = J.start + li;  // list index (row jobs)
       bool store = row_valid;
       int mode_out = 0;  // 0: bf16 to out, 1: fp32 to dense_buf, 2: fp32 to sparse_buf
       long long out_row = 0;
@@ -572,11 +651,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           store = !is_anchor;
         }
       } else if (J.kind == JOB_DENSE_ROWS) {
-        if (li < p.direct_from) {
+        if (gli < p.direct_from) {
           mode_out = 1;
         } else {
           mode_out = 0;
-          out_row = !row_valid ? 0 : (p.out_by_list ? li : list_q_row(p, li));
+          out_row = !row_valid ? 0 : (p.out_by_list ? gli : list_q_row(p, gli));
         }
       } else {
         mode_out = 2;
@@ -587,17 +666,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
                                   : nullptr;
       float* dst_f = (store && mode_out != 0)
                          ? (mode_out == 1 ? p.dense_buf : p.sparse_buf) +
-                               (((long long)J.b * p.n_anchor + li) * p.H + h) * HD
+                               (((long long)J.b * p.n_anchor + gli) * p.H + h) * HD
                          : nullptr;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
-        uint32_t u[32];
-        __syncwarp();  // stores below are per-lane; converge before the collective load
-        tmem_ld32(tO + c * 32, u);
-        tmem_wait_ld();
         float o[32];
+        __syncwarp();  // stores below are per-lane; converge before the collective load
+        tmem_ld32f(tO + c * 32, o);
+        tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(u[e]) * inv_l;
+        for (int e = 0; e < 32; ++e) o[e] *= inv_l;
         if (dst_bf) {
           if (dlt_a) {
 #pragma unroll
@@ -627,7 +705,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(o_empty));
+      if (lane == 0) mbar_arrive(BAR(o_empty[0]) + 8 * q);
     }
   }
 #undef BAR
@@ -653,13 +731,9 @@ __global__ void anchor_delta_kernel(const float* __restrict__ dense, const float
 
 template <int HD>
 static cudaError_t launch_prefill_hd(const PrefillParams& p, int grid, cudaStream_t stream) {
-  static bool attr_set = false;
   const int smem = Geo<HD>::SMEM_BYTES;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  cudaError_t e = cudaFuncSetAttribute(prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
   prefill_kernel<HD><<<grid, NUM_THREADS, smem, stream>>>(p);
   return cudaGetLastError();
 }

@@ -10,6 +10,9 @@ namespace dta {
 
 enum Launch : int { LAUNCH_ROWS = 0, LAUNCH_WINDOW = 1 };
 
+// Query tiles (of 128 rows = R rows x G heads) per kernel job.
+constexpr int PREFILL_NQ = 2;
+
 struct PrefillParams {
   CUtensorMap tm_q;  // (d, s, H, B), box (64, R, G, 1): window launch only
   CUtensorMap tm_k;  // (d, s_kv, Hkv, B), box (64, 128, 1, 1)

@@ -208,6 +208,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 #undef DTA_R8
+#define DTA_F8(i) "=f"(r[i + 0]), "=f"(r[i + 1]), "=f"(r[i + 2]), "=f"(r[i + 3]), "=f"(r[i + 4]), "=f"(r[i + 5]), \
+                  "=f"(r[i + 6]), "=f"(r[i + 7])
+// Same load with the 32 columns landing directly in float registers r[0..31].
+__device__ __forceinline__ void tmem_ld32f(uint32_t taddr, float* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : DTA_F8(0), DTA_F8(8), DTA_F8(16), DTA_F8(24)
+      : "r"(taddr));
+}
+#undef DTA_F8
 #define DTA_W8(i) "r"(r[i + 0]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), \
                   "r"(r[i + 6]), "r"(r[i + 7])
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -228,6 +240,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 #undef DTA_W8
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// per-warpgroup register reallocation (all 4 warps of a warpgroup execute it)
+// ---------------------------------------------------------------------------
+template <int N>
+__device__ __forceinline__ void regs_release() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_acquire() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 // ---------------------------------------------------------------------------
 // math helpers
