@@ -12,7 +12,7 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "_lib", "libdelta_attention_b200.so")
+LIB_PATH = os.environ.get("DTA_LIBRARY") or os.path.join(_HERE, "_lib", "libdelta_attention_b200.so")
 
 ABI_VERSION = 1
 

@@ -88,7 +88,8 @@ inline bool stride_ok(long long s) { return s > 0 && (s * 2) % 16 == 0; }
 // ---------------------------------------------------------------------------
 struct PrefillLayout {
   int s_p, n_anchor, n_sel;
-  size_t buf_bytes;  // one of dense_buf / sparse_buf
+  size_t buf_bytes;    // one of dense_buf / sparse_buf (fp32)
+  size_t delta_bytes;  // delta_buf (bf16)
   size_t ws_bytes;
 };
 
@@ -123,7 +124,8 @@ int prefill_layout(const dta_prefill_args* a, PrefillLayout* L) {
   }
   const bool need_bufs = a->mode == DTA_MODE_DELTA && L->n_anchor > 0;
   L->buf_bytes = need_bufs ? align_up((size_t)a->batch * L->n_anchor * a->n_heads * a->head_dim * 4, 256) : 0;
-  L->ws_bytes = kHeaderBytes + 2 * L->buf_bytes;
+  L->delta_bytes = need_bufs ? align_up((size_t)a->batch * L->n_anchor * a->n_heads * a->head_dim * 2, 256) : 0;
+  L->ws_bytes = kHeaderBytes + 2 * L->buf_bytes + L->delta_bytes;
   return DTA_OK;
 }
 
@@ -195,10 +197,13 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   p.error = reinterpret_cast<int*>(ws) + 1;
   p.dense_buf = L.buf_bytes ? reinterpret_cast<float*>(ws + kHeaderBytes) : nullptr;
   p.sparse_buf = L.buf_bytes ? reinterpret_cast<float*>(ws + kHeaderBytes + L.buf_bytes) : nullptr;
+  __nv_bfloat16* delta_buf =
+      L.delta_bytes ? reinterpret_cast<__nv_bfloat16*>(ws + kHeaderBytes + 2 * L.buf_bytes) : nullptr;
+  p.delta_buf = delta_buf;
 
-  if ((st = encode_4d(&p.tm_k, a->k, d, S, Hkv, B, a->k_stride_s, a->k_stride_h, a->k_stride_b, 128, 1)) != DTA_OK)
+  if ((st = encode_4d(&p.tm_k, a->k, d, S, Hkv, B, a->k_stride_s, a->k_stride_h, a->k_stride_b, dta::PREFILL_BN, 1)) != DTA_OK)
     return st;
-  if ((st = encode_4d(&p.tm_v, a->v, d, S, Hkv, B, a->v_stride_s, a->v_stride_h, a->v_stride_b, 128, 1)) != DTA_OK)
+  if ((st = encode_4d(&p.tm_v, a->v, d, S, Hkv, B, a->v_stride_s, a->v_stride_h, a->v_stride_b, dta::PREFILL_BN, 1)) != DTA_OK)
     return st;
   if ((st = encode_4d(&p.tm_q, a->q, d, S, H, B, a->q_stride_s, a->q_stride_h, a->q_stride_b, R, G)) != DTA_OK)
     return st;
@@ -217,6 +222,13 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
     const int grid = r.n_jobs < sms ? r.n_jobs : sms;
     if ((e = dta::launch_prefill(r, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
   }
+  // delta = dense - sparse per anchor (bf16 for the windowed launch, fp32 telemetry on request)
+  if ((phases & DTA_PHASE_ROWS) && L.buf_bytes) {
+    const long long n = (long long)B * L.n_anchor * H * d;
+    if ((e = dta::launch_anchor_delta(p.dense_buf, p.sparse_buf, delta_buf, a->anchor_delta, n, stream)) !=
+        cudaSuccess)
+      return fail_cuda(e);
+  }
   // launch 2: windowed rows [0, row_end) with the fused delta epilogue
   if (phases & DTA_PHASE_WINDOW) {
     dta::PrefillParams w = p;
@@ -229,11 +241,7 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
       if ((e = dta::launch_prefill(w, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
     }
   }
-  if ((phases & DTA_PHASE_ROWS) && a->anchor_delta && L.buf_bytes) {
-    const long long n = (long long)B * L.n_anchor * H * d;
-    if ((e = dta::launch_anchor_delta(p.dense_buf, p.sparse_buf, a->anchor_delta, n, stream)) != cudaSuccess)
-      return fail_cuda(e);
-  }
+  // (runs between the two launches, stream-ordered)
   return DTA_OK;
 }
 
@@ -284,10 +292,10 @@ int dta_rows(const dta_rows_args* a, void* stream_) {
   p.error = reinterpret_cast<int*>(ws) + 1;
   p.n_dense_tiles = (a->n_rows + JR - 1) / JR;
   p.n_jobs = p.n_dense_tiles * B * Hkv;
-  if ((st = encode_4d(&p.tm_k, a->k, d, a->kv_len, Hkv, B, a->k_stride_s, a->k_stride_h, a->k_stride_b, 128, 1)) !=
+  if ((st = encode_4d(&p.tm_k, a->k, d, a->kv_len, Hkv, B, a->k_stride_s, a->k_stride_h, a->k_stride_b, dta::PREFILL_BN, 1)) !=
       DTA_OK)
     return st;
-  if ((st = encode_4d(&p.tm_v, a->v, d, a->kv_len, Hkv, B, a->v_stride_s, a->v_stride_h, a->v_stride_b, 128, 1)) !=
+  if ((st = encode_4d(&p.tm_v, a->v, d, a->kv_len, Hkv, B, a->v_stride_s, a->v_stride_h, a->v_stride_b, dta::PREFILL_BN, 1)) !=
       DTA_OK)
     return st;
   cudaError_t e = cudaMemsetAsync(a->workspace, 0, kHeaderBytes, stream);

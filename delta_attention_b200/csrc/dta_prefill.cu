@@ -24,10 +24,14 @@
 //   warps 2, 3  : idle
 //   warps 4..7  : softmax + epilogue of tile A, one thread per row (TMEM lane)
 //   warps 8..11 : softmax + epilogue of tile B
-// MMA issue order per key tile i:  PV_A(i), S_A(i+1), PV_B(i), S_B(i+1), so the
-// softmax of one tile overlaps the matrix products of the other.
-// TMEM: S_A, S_B (128 fp32 columns each; P is written back over S as packed
-// bf16 and read by the TS-form MMA), O_A, O_B (head_dim columns each).
+// With 128-key tiles each query tile has one S buffer in TMEM and the MMA
+// issue order per key tile i is PV_A(i), S_A(i+1), PV_B(i), S_B(i+1), so the
+// softmax of one query tile overlaps the matrix products of the other.  With
+// 64-key tiles (PREFILL_BN = 64) each query tile has two S buffers and the
+// order is PV_A(i), S_A(i+2), PV_B(i), S_B(i+2).
+// TMEM (512 columns): the S buffers (BN fp32 columns each; P is written back
+// over the first BN/2 columns of its S buffer as packed bf16 and read by the
+// TS-form MMA), then O_A, O_B (head_dim columns each) from column 256.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -41,7 +45,8 @@
 namespace dta {
 
 constexpr int BM = 128;
-constexpr int BN = 128;
+constexpr int BN = PREFILL_BN;  // keys per tile
+constexpr int S_BUFS = (BN == 64) ? 2 : 1;  // S buffers per query tile
 constexpr int NUM_THREADS = 128 + PREFILL_NQ * 128;
 // Register split: launched at 168 per thread (384 x 168 = 64512), the control
 // warpgroup drops to 56 and the softmax warpgroups rise to 224:
@@ -52,27 +57,36 @@ static_assert(128 * REGS_CONTROL + PREFILL_NQ * 128 * REGS_SOFTMAX <= NUM_THREAD
 constexpr int CTRL_BYTES = 1024;
 constexpr int Q_SLOTS = 3;  // rotating Q tile slots: the next job's Q loads overlap this job
 constexpr int NQ = PREFILL_NQ;
+// Element pairs (of the 16 per 32-column chunk) whose exponentials run on the
+// FMA pipe (exp2_poly) instead of the MUFU unit.
+#ifndef DTA_POLY_PAIRS
+#define DTA_POLY_PAIRS 0
+#endif
+constexpr int POLY_PAIRS = DTA_POLY_PAIRS;
 
 template <int HD>
 struct Geo {
   static constexpr int REGIONS = HD / 64;           // 128-byte swizzle atoms along head_dim
-  static constexpr int REGION_BYTES = 128 * 128;    // 128 rows x 128 bytes
-  static constexpr int TILE_BYTES = REGIONS * REGION_BYTES;  // one 128 x HD bf16 tile
-  static constexpr int KV_STAGES = (HD == 128) ? 2 : 4;
+  static constexpr int REGION_BYTES = 128 * 128;    // Q: 128 rows x 128 bytes
+  static constexpr int TILE_BYTES = REGIONS * REGION_BYTES;  // one 128 x HD bf16 Q tile
+  static constexpr int KV_REGION_BYTES = BN * 128;  // K/V: BN rows x 128 bytes
+  static constexpr int KV_TILE_BYTES = REGIONS * KV_REGION_BYTES;
+  static constexpr int KV_STAGES = (BN == 64) ? 4 : 2;
   static constexpr int Q_OFF = CTRL_BYTES;
   static constexpr int K_OFF = Q_OFF + Q_SLOTS * TILE_BYTES;
-  static constexpr int V_OFF = K_OFF + KV_STAGES * TILE_BYTES;
-  static constexpr int SMEM_BYTES = V_OFF + KV_STAGES * TILE_BYTES + 1024;  // + alignment slack
+  static constexpr int V_OFF = K_OFF + KV_STAGES * KV_TILE_BYTES;
+  static constexpr int SMEM_BYTES = V_OFF + KV_STAGES * KV_TILE_BYTES + 1024;  // + alignment slack
   static constexpr int TMEM_COLS = 512;
-  static constexpr int S_COL = 0;    // S of tile q at q * 128
+  static constexpr int S_COL = 0;    // S buffer b of tile q at (q * S_BUFS + b) * BN
   static constexpr int O_COL = 256;  // O of tile q at 256 + q * 128
 };
+static_assert(Geo<128>::SMEM_BYTES <= 232448, "shared memory budget");
 
 struct Ctrl {
   uint64_t job_full[2], job_empty[2];
   uint64_t q_full[Q_SLOTS], q_empty[Q_SLOTS];
   uint64_t k_full[4], k_empty[4], v_full[4], v_empty[4];
-  uint64_t s_full[NQ], p_full[NQ], o_full[NQ], o_empty[NQ];
+  uint64_t s_full[NQ * S_BUFS], p_full[NQ * S_BUFS], o_full[NQ], o_empty[NQ];
   uint64_t drain;
   int job[2][8];
   uint32_t tmem_base;
@@ -239,8 +253,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       mbar_init(BAR(v_empty[0]) + 8 * i, 1);
     }
     for (int q = 0; q < NQ; ++q) {
-      mbar_init(BAR(s_full[0]) + 8 * q, 1);
-      mbar_init(BAR(p_full[0]) + 8 * q, 4);
+      for (int b = 0; b < S_BUFS; ++b) {
+        mbar_init(BAR(s_full[0]) + 8 * (q * S_BUFS + b), 1);
+        mbar_init(BAR(p_full[0]) + 8 * (q * S_BUFS + b), 4);
+      }
       mbar_init(BAR(o_full[0]) + 8 * q, 1);
       mbar_init(BAR(o_empty[0]) + 8 * q, 4);
     }
@@ -268,8 +284,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   if (warp < 4) {
   if (warp == 0) {
     // ======================= producer =======================
-    int n = 0;      // K/V tiles issued so far (ring position)
-    int qload = 0;  // Q tiles loaded so far (slot = qload % Q_SLOTS)
+    int n = 0;                // K/V tiles issued so far (ring position)
+    int qfree = 1;            // the Q slot tile B takes next (1 or 2)
+    int qfills[Q_SLOTS] = {0, 0, 0};
     bool ok = true;
     for (int it = 0; ok; ++it) {
       const int slot = it & 1;
@@ -292,17 +309,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       }
       if (J.kind == JOB_END) break;
       const Plan P = make_plan(p, J);
-      // ---- Q tiles ----
-      for (int q = 0; q < NQ; ++q) {
-        if (P.tiles_t[q] == 0) continue;
-        const int qs = qload % Q_SLOTS;
+      // Q slot rotation (mirrored by the MMA issuer): tile A keeps slot 0, which
+      // the previous job's tile A frees at its last S; tile B takes the free
+      // slot; the previous B slot becomes the free one.  Loads go in the order
+      // Q_B, K0, V0, Q_A, K1, V1, ... so the next job's first tiles are not
+      // queued behind the wait for slot 0.
+      const int sl[NQ] = {0, qfree};
+      qfree = 3 - qfree;
+      auto load_q = [&](int q) -> bool {
+        if (P.tiles_t[q] == 0) return true;
+        const int qs = sl[q];
         const uint32_t qbuf = q_u32 + (uint32_t)qs * G::TILE_BYTES;
-        if (!mbar_wait_warp(BAR(q_empty[0]) + 8 * qs, ((qload / Q_SLOTS) & 1) ^ 1, abort_flag, err,
-                            KERR_TIMEOUT_PRODUCER)) {
-          ok = false;
-          break;
-        }
-        ++qload;
+        if (!mbar_wait_warp(BAR(q_empty[0]) + 8 * qs, (qfills[qs] & 1) ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER))
+          return false;
+        ++qfills[qs];
         if (J.kind == JOB_WINDOW) {
           if (lane == 0) {
             mbar_arrive_expect_tx(BAR(q_full[0]) + 8 * qs, G::TILE_BYTES);
@@ -332,9 +352,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           __syncwarp();
           if (lane == 0) mbar_arrive(BAR(q_full[0]) + 8 * qs);
         }
-      }
-      if (!ok) break;
-      // ---- K and V tiles ----
+        return true;
+      };
+      if (!load_q(1)) break;
+      // ---- K and V tiles (Q_A after the first pair) ----
       for (int i = 0; i < P.n_tiles; ++i, ++n) {
         const int st = n % G::KV_STAGES;
         const uint32_t ph = (uint32_t)((n / G::KV_STAGES) & 1);
@@ -344,20 +365,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           break;
         }
         if (lane == 0) {
-          const uint32_t kdst = k_u32 + (uint32_t)st * G::TILE_BYTES;
-          mbar_arrive_expect_tx(BAR(k_full[0]) + 8 * st, G::TILE_BYTES);
+          const uint32_t kdst = k_u32 + (uint32_t)st * G::KV_TILE_BYTES;
+          mbar_arrive_expect_tx(BAR(k_full[0]) + 8 * st, G::KV_TILE_BYTES);
           for (int r = 0; r < G::REGIONS; ++r)
-            tma_load_4d(kdst + r * G::REGION_BYTES, &p.tm_k, BAR(k_full[0]) + 8 * st, r * 64, ks, J.g, J.b);
+            tma_load_4d(kdst + r * G::KV_REGION_BYTES, &p.tm_k, BAR(k_full[0]) + 8 * st, r * 64, ks, J.g, J.b);
         }
         if (!mbar_wait_warp(BAR(v_empty[0]) + 8 * st, ph ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
         }
         if (lane == 0) {
-          const uint32_t vdst = v_u32 + (uint32_t)st * G::TILE_BYTES;
-          mbar_arrive_expect_tx(BAR(v_full[0]) + 8 * st, G::TILE_BYTES);
+          const uint32_t vdst = v_u32 + (uint32_t)st * G::KV_TILE_BYTES;
+          mbar_arrive_expect_tx(BAR(v_full[0]) + 8 * st, G::KV_TILE_BYTES);
           for (int r = 0; r < G::REGIONS; ++r)
-            tma_load_4d(vdst + r * G::REGION_BYTES, &p.tm_v, BAR(v_full[0]) + 8 * st, r * 64, ks, J.g, J.b);
+            tma_load_4d(vdst + r * G::KV_REGION_BYTES, &p.tm_v, BAR(v_full[0]) + 8 * st, r * 64, ks, J.g, J.b);
+        }
+        if (i == 0 && !load_q(0)) {
+          ok = false;
+          break;
         }
       }
     }
@@ -377,14 +402,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     if (lane == 0) {
       constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, BN, 0);
       constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, HD, 1);
+      // base descriptors: Q slot 0 / K stage 0 (K-major), V stage 0 (MN-major)
+      const uint64_t qdesc0 = smem_desc_sw128(q_u32, 16, 1024);
+      const uint64_t kdesc0 = smem_desc_sw128(k_u32, 16, 1024);
+      const uint64_t vdesc0 = smem_desc_sw128(v_u32, G::KV_REGION_BYTES, 1024);
       int n = 0;                // K/V tiles consumed so far (ring position)
-      int qload = 0;            // Q tiles consumed so far (slot position)
-      int cnt_s[NQ] = {0, 0};   // S tiles issued per query tile (= PVs)
+      int qfree = 1;            // Q slot of the next job's tile B
+      int quses[Q_SLOTS] = {0, 0, 0};
+      int cnt_s[NQ] = {0, 0};   // S tiles issued per query tile
+      int cnt_pv[NQ] = {0, 0};  // PV products issued per query tile
       int jobs_t[NQ] = {0, 0};  // jobs in which query tile q was active
       bool aborted = false;
       for (int it = 0; !aborted; ++it) {
         const int slot = it & 1;
-        if (!mbar_wait(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) break;
+        if (!mbar_poll(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) break;
         Job J;
         {
           const volatile int* src = ctrl->job[slot];
@@ -393,73 +424,81 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         mbar_arrive(BAR(job_empty[0]) + 8 * slot);
         if (J.kind == JOB_END) break;
         const Plan P = make_plan(p, J);
+        // Q slots: same rotation as the producer (tile A slot 0, tile B the free slot)
         uint32_t qbuf[NQ];
-        int qslot[NQ];
-        for (int q = 0; q < NQ; ++q) {
-          qbuf[q] = 0;
-          qslot[q] = 0;
-          if (P.tiles_t[q] == 0) continue;
-          qslot[q] = qload % Q_SLOTS;
-          qbuf[q] = q_u32 + (uint32_t)qslot[q] * G::TILE_BYTES;
-          if (!mbar_wait(BAR(q_full[0]) + 8 * qslot[q], (qload / Q_SLOTS) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) {
-            aborted = true;
-            break;
-          }
-          ++qload;
-        }
-        if (aborted) break;
+        int qslot[NQ] = {0, qfree};
+        qfree = 3 - qfree;
+        bool qready[NQ] = {false, false};
+        for (int q = 0; q < NQ; ++q) qbuf[q] = q_u32 + (uint32_t)qslot[q] * G::TILE_BYTES;
+        auto wait_q = [&](int q) -> bool {
+          if (qready[q] || P.tiles_t[q] == 0) return true;
+          const int qs = qslot[q];
+          if (!mbar_poll(BAR(q_full[0]) + 8 * qs, quses[qs] & 1, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
+          ++quses[qs];
+          qready[q] = true;
+          return true;
+        };
         const int n0 = n;  // ring position of this job's key tile 0
         // the last query tile active at key tile i releases K_i / V_i
         auto last_active = [&](int i) { return (i < P.tiles_t[NQ - 1]) ? NQ - 1 : 0; };
         // S_q(i) = Q_q . K_i^T
         auto issue_s = [&](int q, int i) -> bool {
           const int m = n0 + i, st = m % G::KV_STAGES;
+          if (i == 0 && !wait_q(q)) return false;
           if (q == 0 || i >= P.tiles_t[0]) {  // first user of K_i waits for it
-            if (!mbar_wait(BAR(k_full[0]) + 8 * st, (m / G::KV_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+            if (!mbar_poll(BAR(k_full[0]) + 8 * st, (m / G::KV_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
               return false;
           }
           tc_fence_after();
-          const uint32_t tS = tmem + G::S_COL + q * 128;
-          const uint32_t kbase = k_u32 + (uint32_t)st * G::TILE_BYTES;
+          const int sb = cnt_s[q] % S_BUFS;  // S buffer
+          const uint32_t tS = tmem + G::S_COL + (q * S_BUFS + sb) * BN;
+          // descriptors differ only in the 14-bit start-address field, which
+          // never carries out (shared memory < 256 KB), so offsets are plain adds
+          const uint64_t qd = qdesc0 + ((qbuf[q] - q_u32) >> 4);
+          const uint64_t kd = kdesc0 + (((uint32_t)st * G::KV_TILE_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * G::REGION_BYTES + (kk & 3) * 32;
-            umma_ss(tS, smem_desc_sw128(qbuf[q] + off, 16, 1024), smem_desc_sw128(kbase + off, 16, 1024), IDESC_QK,
-                    kk > 0 ? 1u : 0u);
+            const uint32_t qoff = ((kk >> 2) * G::REGION_BYTES + (kk & 3) * 32) >> 4;
+            const uint32_t koff = ((kk >> 2) * G::KV_REGION_BYTES + (kk & 3) * 32) >> 4;
+            umma_ss(tS, qd + qoff, kd + koff, IDESC_QK, kk > 0 ? 1u : 0u);
           }
-          umma_commit(BAR(s_full[0]) + 8 * q);
+          umma_commit(BAR(s_full[0]) + 8 * (q * S_BUFS + sb));
           ++cnt_s[q];
           if (q == last_active(i)) umma_commit(BAR(k_empty[0]) + 8 * st);
           if (i == P.tiles_t[q] - 1) umma_commit(BAR(q_empty[0]) + 8 * qslot[q]);
           return true;
         };
-        // O_q += P_q(i) . V_i   (S_q(i) is the last S issued for q at this point)
+        // O_q += P_q(i) . V_i
         auto issue_pv = [&](int q, int i) -> bool {
           const int m = n0 + i, st = m % G::KV_STAGES;
-          if (!mbar_wait(BAR(p_full[0]) + 8 * q, (cnt_s[q] - 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
+          const int pb = cnt_pv[q] % S_BUFS;  // S/P buffer of tile i
+          if (!mbar_poll(BAR(p_full[0]) + 8 * (q * S_BUFS + pb), (cnt_pv[q] / S_BUFS) & 1, abort_flag, err,
+                         KERR_TIMEOUT_MMA))
+            return false;
           if (i == 0 && jobs_t[q] > 0) {
-            if (!mbar_wait(BAR(o_empty[0]) + 8 * q, (jobs_t[q] - 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+            if (!mbar_poll(BAR(o_empty[0]) + 8 * q, (jobs_t[q] - 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
               return false;
           }
           if (q == 0 || i >= P.tiles_t[0]) {  // first user of V_i waits for it
-            if (!mbar_wait(BAR(v_full[0]) + 8 * st, (m / G::KV_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+            if (!mbar_poll(BAR(v_full[0]) + 8 * st, (m / G::KV_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
               return false;
           }
           tc_fence_after();
-          const uint32_t tP = tmem + G::S_COL + q * 128;
+          const uint32_t tP = tmem + G::S_COL + (q * S_BUFS + pb) * BN;
           const uint32_t tO = tmem + G::O_COL + q * 128;
-          const uint32_t vbase = v_u32 + (uint32_t)st * G::TILE_BYTES;
+          const uint64_t vd = vdesc0 + (((uint32_t)st * G::KV_TILE_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)
-            umma_ts(tO, tP + kk * 8, smem_desc_sw128(vbase + kk * 2048, G::REGION_BYTES, 1024), IDESC_PV,
-                    (i == 0 && kk == 0) ? 0u : 1u);
+            umma_ts(tO, tP + kk * 8, vd + ((kk * 2048) >> 4), IDESC_PV, (i == 0 && kk == 0) ? 0u : 1u);
           umma_commit(BAR(o_full[0]) + 8 * q);
+          ++cnt_pv[q];
           if (q == last_active(i)) umma_commit(BAR(v_empty[0]) + 8 * st);
           return true;
         };
-        // prologue: S of key tile 0 for every active query tile
-        for (int q = 0; q < NQ && !aborted; ++q)
-          if (P.tiles_t[q] > 0 && !issue_s(q, 0)) aborted = true;
+        // prologue: S of the first S_BUFS key tiles for every active query tile
+        for (int i = 0; i < S_BUFS && !aborted; ++i)
+          for (int q = 0; q < NQ && !aborted; ++q)
+            if (i < P.tiles_t[q] && !issue_s(q, i)) aborted = true;
         for (int i = 0; i < P.n_tiles && !aborted; ++i) {
           for (int q = 0; q < NQ; ++q) {
             if (i >= P.tiles_t[q]) continue;
@@ -467,7 +506,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
               aborted = true;
               break;
             }
-            if (i + 1 < P.tiles_t[q] && !issue_s(q, i + 1)) {
+            if (i + S_BUFS < P.tiles_t[q] && !issue_s(q, i + S_BUFS)) {
               aborted = true;
               break;
             }
@@ -496,7 +535,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     const int r = quarter * 32 + lane;    // row of this thread inside its query tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int hh = r / p.R, rr = r - (r / p.R) * p.R;
-    const uint32_t tS = tmem + lane_off + G::S_COL + q * 128;
+    const uint32_t tS0 = tmem + lane_off + G::S_COL + q * S_BUFS * BN;
     const uint32_t tO = tmem + lane_off + G::O_COL + q * 128;
     const float sl2 = p.scale_log2;
     int cnt = 0;  // S tiles consumed by this warpgroup (= PVs of its query tile)
@@ -526,7 +565,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       float m_run = -INFINITY, l_run = 0.f;
       bool aborted = false;
       for (int i = 0; i < T; ++i, ++cnt) {
-        if (!mbar_wait_warp(BAR(s_full[0]) + 8 * q, cnt & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
+        const int sb = cnt % S_BUFS;  // S buffer of this tile
+        const uint32_t tS = tS0 + sb * BN;
+        if (!mbar_wait_warp(BAR(s_full[0]) + 8 * (q * S_BUFS + sb), (cnt / S_BUFS) & 1, abort_flag, err,
+                            KERR_TIMEOUT_SOFTMAX)) {
           aborted = true;
           break;
         }
@@ -553,25 +595,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
             x[e] = v ? x[e] : -INFINITY;
           }
         }
-        float mt = -INFINITY;
+        // row max: 8 independent chains of three-input maxima
+        float mk[8];
 #pragma unroll
-        for (int e = 0; e < BN; ++e) mt = fmaxf(mt, x[e]);
+        for (int k = 0; k < 8; ++k) {
+          float m = fmax3(x[k], x[k + 8], x[k + 16]);
+#pragma unroll
+          for (int j = 3; j + 1 < BN / 8; j += 2) m = fmax3(m, x[k + 8 * j], x[k + 8 * (j + 1)]);
+          mk[k] = fmaxf(m, x[k + BN - 8]);
+        }
+        float mt = fmax3(fmax3(mk[0], mk[1], mk[2]), fmax3(mk[3], mk[4], mk[5]), fmaxf(mk[6], mk[7]));
         mt *= sl2;  // scaled units (log2 domain); -inf stays -inf
         // keep the running max unless it grows by more than 2^8 (exact: O and
         // l always share the reference max; P stays <= 256)
         const bool need = (i > 0) && (mt > m_run + 8.0f);
         const float m_new = (i == 0 || need) ? mt : m_run;
         const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        float lsum = 0.f;
+        // P = exp2(S * scale - m): scale/shift and row sums on packed fp32 pairs
+        const uint64_t sc2 = f2_pack(sl2, sl2);
+        const uint64_t nm2 = f2_pack(-m_use, -m_use);
+        uint64_t ls2[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ls2[k] = f2_pack(0.f, 0.f);
         __syncwarp();  // converge before the warp-collective TMEM stores
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const float p0 = fast_exp2(fmaf(x[c * 32 + 2 * e], sl2, -m_use));
-            const float p1 = fast_exp2(fmaf(x[c * 32 + 2 * e + 1], sl2, -m_use));
-            lsum += p0 + p1;
+            float a0, a1;
+            f2_unpack(f2_fma(f2_pack(x[c * 32 + 2 * e], x[c * 32 + 2 * e + 1]), sc2, nm2), a0, a1);
+            // spread the polynomial pairs evenly over the chunk
+            const bool poly = POLY_PAIRS > 0 && (e % 16) * POLY_PAIRS % 16 >= 16 - POLY_PAIRS;
+            const float p0 = poly ? exp2_poly(a0) : fast_exp2(a0);
+            const float p1 = poly ? exp2_poly(a1) : fast_exp2(a1);
+            ls2[e & 3] = f2_add(ls2[e & 3], f2_pack(p0, p1));
             pk[e] = pack_bf16x2(p0, p1);
           }
           tmem_st16(tS + c * 16, pk);
@@ -601,24 +659,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           }
         }
         m_run = m_new;
-        l_run += lsum;
+        {
+          float l0, l1, l2, l3;
+          f2_unpack(f2_add(f2_add(ls2[0], ls2[1]), f2_add(ls2[2], ls2[3])), l0, l1);
+          (void)l2;
+          (void)l3;
+          l_run += l0 + l1;
+        }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(BAR(p_full[0]) + 8 * q);
+        if (lane == 0) mbar_arrive(BAR(p_full[0]) + 8 * (q * S_BUFS + sb));
       }
       if (aborted) break;
-      // ---- epilogue: wait for the last PV, normalise, correct, store ----
-      if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, (cnt - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
-      tc_fence_after();
-      const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
+      // ---- epilogue: normalise, correct, store ----
       const int h = J.g * p.G + hh;
       const int gli = J.start + li;  // list index (row jobs)
       bool store = row_valid;
       int mode_out = 0;  // 0: bf16 to out, 1: fp32 to dense_buf, 2: fp32 to sparse_buf
       long long out_row = 0;
-      const float* dlt_a = nullptr;
-      const float* dlt_b = nullptr;
+      const __nv_bfloat16* dlt = nullptr;
       if (J.kind == JOB_WINDOW) {
         out_row = qpos;
         if (store && p.mode == 0) {
@@ -633,9 +693,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           } else {
             a = qpos / p.gamma;
           }
-          const long long off = (((long long)J.b * p.n_anchor + a) * p.H + h) * HD;
-          dlt_a = p.dense_buf + off;
-          dlt_b = p.sparse_buf + off;
+          dlt = p.delta_buf + (((long long)J.b * p.n_anchor + a) * p.H + h) * HD;
         } else if (store && p.mode == 1) {
           bool is_anchor;
           if (p.anchors) {
@@ -660,6 +718,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       } else {
         mode_out = 2;
       }
+      // the owning anchor's delta row (bf16) is fetched in one batch of 16-byte
+      // loads before waiting for the last PV, so its latency overlaps that wait
+      uint4 dv[HD / 8];
+      if (dlt) {
+#pragma unroll
+        for (int c = 0; c < HD / 8; ++c) dv[c] = reinterpret_cast<const uint4*>(dlt)[c];
+      }
+      if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, (cnt - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
+      tc_fence_after();
+      const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
       // TMEM reads are warp-collective: every lane loads, stores are predicated
       __nv_bfloat16* dst_bf = (store && mode_out == 0)
                                   ? p.out + (((long long)J.b * p.out_rows + out_row) * p.H + h) * HD
@@ -677,25 +745,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] *= inv_l;
         if (dst_bf) {
-          if (dlt_a) {
+          if (dlt) {
 #pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              const float4 da = *reinterpret_cast<const float4*>(dlt_a + c * 32 + e);
-              const float4 db = *reinterpret_cast<const float4*>(dlt_b + c * 32 + e);
-              o[e + 0] += da.x - db.x;
-              o[e + 1] += da.y - db.y;
-              o[e + 2] += da.z - db.z;
-              o[e + 3] += da.w - db.w;
+            for (int v4 = 0; v4 < 4; ++v4) {
+              const uint4 w = dv[c * 4 + v4];
+              const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                o[v4 * 8 + 2 * k] += __uint_as_float(ww[k] << 16);
+                o[v4 * 8 + 2 * k + 1] += __uint_as_float(ww[k] & 0xffff0000u);
+              }
             }
           }
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 w;
-            w.x = pack_bf16x2(o[e + 0], o[e + 1]);
-            w.y = pack_bf16x2(o[e + 2], o[e + 3]);
-            w.z = pack_bf16x2(o[e + 4], o[e + 5]);
-            w.w = pack_bf16x2(o[e + 6], o[e + 7]);
-            *reinterpret_cast<uint4*>(dst_bf + c * 32 + e) = w;
+          for (int e = 0; e < 32; e += 16) {
+            uint32_t w[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) w[k] = pack_bf16x2(o[e + 2 * k], o[e + 2 * k + 1]);
+            st_global_v8(dst_bf + c * 32 + e, w);
           }
         } else if (dst_f) {
 #pragma unroll
@@ -705,7 +772,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(o_empty[0]) + 8 * q);
+      if (lane == 0) mbar_arrive_relaxed(BAR(o_empty[0]) + 8 * q);
     }
   }
 #undef BAR
@@ -719,13 +786,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   }
 }
 
-// anchor_delta[b, a, h, :] = dense_buf - sparse_buf (fp32), optional telemetry output
+// delta[b, a, h, :] = dense_buf - sparse_buf: bf16 for the windowed launch,
+// optionally fp32 for telemetry
 __global__ void anchor_delta_kernel(const float* __restrict__ dense, const float* __restrict__ sparse,
-                                    float* __restrict__ out, long long n4) {
+                                    __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32, long long n4) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
     const float4 a = reinterpret_cast<const float4*>(dense)[i];
     const float4 b = reinterpret_cast<const float4*>(sparse)[i];
-    reinterpret_cast<float4*>(out)[i] = make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
+    const float4 d = make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
+    uint2 w;
+    w.x = pack_bf16x2(d.x, d.y);
+    w.y = pack_bf16x2(d.z, d.w);
+    reinterpret_cast<uint2*>(out_bf16)[i] = w;
+    if (out_f32) reinterpret_cast<float4*>(out_f32)[i] = d;
   }
 }
 
@@ -743,12 +816,13 @@ cudaError_t launch_prefill(const PrefillParams& p, int head_dim, int grid, cudaS
   return launch_prefill_hd<64>(p, grid, stream);
 }
 
-cudaError_t launch_anchor_delta(const float* dense, const float* sparse, float* out, long long n, cudaStream_t s) {
+cudaError_t launch_anchor_delta(const float* dense, const float* sparse, __nv_bfloat16* delta_bf16, float* delta_f32,
+                                long long n, cudaStream_t s) {
   const long long n4 = n / 4;
   int blocks = (int)((n4 + 255) / 256);
   if (blocks > 4096) blocks = 4096;
   if (blocks < 1) blocks = 1;
-  anchor_delta_kernel<<<blocks, 256, 0, s>>>(dense, sparse, out, n4);
+  anchor_delta_kernel<<<blocks, 256, 0, s>>>(dense, sparse, delta_bf16, delta_f32, n4);
   return cudaGetLastError();
 }
 

@@ -12,6 +12,8 @@ enum Launch : int { LAUNCH_ROWS = 0, LAUNCH_WINDOW = 1 };
 
 // Query tiles (of 128 rows = R rows x G heads) per kernel job.
 constexpr int PREFILL_NQ = 2;
+// Keys per K/V tile (the TMA box height of the K and V tensor maps).
+constexpr int PREFILL_BN = 128;
 
 struct PrefillParams {
   CUtensorMap tm_q;  // (d, s, H, B), box (64, R, G, 1): window launch only
@@ -38,11 +40,14 @@ struct PrefillParams {
   int* error;                   // kernel error word, zeroed by the host
   float* dense_buf;             // [B, n_anchor, H, d] fp32
   float* sparse_buf;            // [B, n_anchor, H, d] fp32
+  const __nv_bfloat16* delta_buf;  // [B, n_anchor, H, d] bf16: dense - sparse (window launch)
   __nv_bfloat16* out;           // [B, out_rows, H, d]
 };
 
 cudaError_t launch_prefill(const PrefillParams& p, int head_dim, int grid, cudaStream_t stream);
-cudaError_t launch_anchor_delta(const float* dense, const float* sparse, float* out, long long n,
-                                cudaStream_t stream);
+// delta = dense - sparse per anchor: bf16 into delta_bf16 (for the windowed
+// launch) and, when delta_f32 is not null, fp32 into delta_f32 (telemetry).
+cudaError_t launch_anchor_delta(const float* dense, const float* sparse, __nv_bfloat16* delta_bf16, float* delta_f32,
+                                long long n, cudaStream_t stream);
 
 }  // namespace dta

@@ -45,6 +45,12 @@ __device__ __forceinline__ void mbar_init_fence() {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
+// Arrive without release semantics: the arriving thread's earlier global
+// stores are not waited for.  Used where the consumer only depends on TMEM
+// accesses that tcgen05 fences already order.
+__device__ __forceinline__ void mbar_arrive_relaxed(uint32_t bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
@@ -84,6 +90,43 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
                                           int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   return mbar_wait_slow(bar, parity, abort_flag, err, code);
+}
+
+// Polling variant for latency-critical single-thread waiters (the MMA issuer):
+// mbarrier.test_wait never suspends, so the phase completion is seen within a
+// few cycles instead of after try_wait's suspend interval.  Same bound and
+// abort protocol as mbar_wait.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+static __device__ __noinline__ bool mbar_poll_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                   int* err, int code) {
+  const long long t0 = clock64();
+  uint32_t it = 0;
+  while (true) {
+    if (mbar_test(bar, parity)) return true;
+    if ((++it & 1023u) == 0u) {
+      if (*abort_flag) return false;
+      if (clock64() - t0 > kWaitTimeoutCycles) {
+        *abort_flag = 1;
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ bool mbar_poll(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int code) {
+  if (mbar_test(bar, parity)) return true;
+  return mbar_poll_slow(bar, parity, abort_flag, err, code);
 }
 
 // Warp-collective variant: every lane waits, then the warp reconverges so the
@@ -261,6 +304,58 @@ __device__ __forceinline__ float fast_exp2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// three-input maximum (one instruction on sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// packed fp32 pairs (one instruction operates on both halves)
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// 2^x evaluated on the FMA pipe instead of the MUFU unit.  Range reduction
+// x = n + f with n = rint(x) (the 1.5 * 2^23 shifter leaves rint(x) in the low
+// mantissa bits of t) and |f| <= 1/2; 2^f from a degree-3 polynomial whose
+// coefficients minimise the maximum relative error on [-1/2, 1/2] (computed
+// for this kernel with the Remez exchange algorithm: 7.5e-5 in exact arithmetic,
+// 1.5e-4 in fp32 over [-126, 8], against bf16 rounding of P at 2e-3); 2^n is
+// applied by adding n to the exponent field.  Inputs below -126 are clamped
+// (the result is then a negligible tiny number, never NaN).
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float t = __fadd_rn(x, 12582912.0f);
+  const float n = __fsub_rn(t, 12582912.0f);
+  const float f = __fsub_rn(x, n);
+  float p = __fmaf_rn(0.05517166905792616f, f, 0.2426111221932161f);
+  p = __fmaf_rn(p, f, 0.6932609854606553f);
+  p = __fmaf_rn(p, f, 0.9999280735394012f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// 32-byte global store (one sector per lane)
+__device__ __forceinline__ void st_global_v8(void* ptr, const uint32_t (&v)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(ptr), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+               "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));

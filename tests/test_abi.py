@@ -66,7 +66,8 @@ def test_workspace_size_query():
     L = _lib.lib()
     a = _prefill_args(seq_len=131072)
     n_anchor = (131072 - 128) // 64
-    expect = 256 + 2 * ((1 * n_anchor * 32 * 128 * 4 + 255) // 256 * 256)
+    expect = 256 + 2 * ((1 * n_anchor * 32 * 128 * 4 + 255) // 256 * 256) \
+        + (1 * n_anchor * 32 * 128 * 2 + 255) // 256 * 256  # fp32 dense + sparse, bf16 delta
     assert L.dta_prefill_workspace_size(ctypes.byref(a)) == expect
     a.mode = 2  # sparse-only needs only the header
     assert L.dta_prefill_workspace_size(ctypes.byref(a)) == 256
