@@ -48,12 +48,6 @@ constexpr int BM = 128;
 constexpr int BN = PREFILL_BN;  // keys per tile
 constexpr int S_BUFS = (BN == 64) ? 2 : 1;  // S buffers per query tile
 constexpr int NUM_THREADS = 128 + PREFILL_NQ * 128;
-// Register split: launched at 168 per thread (384 x 168 = 64512), the control
-// warpgroup drops to 56 and the softmax warpgroups rise to 224:
-// 128 * 56 + 256 * 224 = 64512.
-constexpr int REGS_CONTROL = 104;
-constexpr int REGS_SOFTMAX = 200;
-static_assert(128 * REGS_CONTROL + PREFILL_NQ * 128 * REGS_SOFTMAX <= NUM_THREADS * 168, "register split");
 constexpr int CTRL_BYTES = 1024;
 constexpr int Q_SLOTS = 3;  // rotating Q tile slots: the next job's Q loads overlap this job
 constexpr int NQ = PREFILL_NQ;
@@ -86,7 +80,8 @@ struct Ctrl {
   uint64_t job_full[2], job_empty[2];
   uint64_t q_full[Q_SLOTS], q_empty[Q_SLOTS];
   uint64_t k_full[4], k_empty[4], v_full[4], v_empty[4];
-  uint64_t s_full[NQ * S_BUFS], p_full[NQ * S_BUFS], o_full[NQ], o_empty[NQ];
+  // p_full[2 * (q * S_BUFS + b) + h]: half h of P (keys [h * BN/2, (h+1) * BN/2))
+  uint64_t s_full[NQ * S_BUFS], p_full[NQ * S_BUFS * 2], o_full[NQ], o_empty[NQ];
   uint64_t drain;
   int job[2][8];
   uint32_t tmem_base;
@@ -255,7 +250,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     for (int q = 0; q < NQ; ++q) {
       for (int b = 0; b < S_BUFS; ++b) {
         mbar_init(BAR(s_full[0]) + 8 * (q * S_BUFS + b), 1);
-        mbar_init(BAR(p_full[0]) + 8 * (q * S_BUFS + b), 4);
+        mbar_init(BAR(p_full[0]) + 8 * (2 * (q * S_BUFS + b)), 4);
+        mbar_init(BAR(p_full[0]) + 8 * (2 * (q * S_BUFS + b) + 1), 4);
       }
       mbar_init(BAR(o_full[0]) + 8 * q, 1);
       mbar_init(BAR(o_empty[0]) + 8 * q, 4);
@@ -468,13 +464,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           if (i == P.tiles_t[q] - 1) umma_commit(BAR(q_empty[0]) + 8 * qslot[q]);
           return true;
         };
-        // O_q += P_q(i) . V_i
+        // O_q += P_q(i) . V_i, in two halves of the key tile: the first half
+        // of P is released while the softmax still computes the second
         auto issue_pv = [&](int q, int i) -> bool {
           const int m = n0 + i, st = m % G::KV_STAGES;
           const int pb = cnt_pv[q] % S_BUFS;  // S/P buffer of tile i
-          if (!mbar_poll(BAR(p_full[0]) + 8 * (q * S_BUFS + pb), (cnt_pv[q] / S_BUFS) & 1, abort_flag, err,
-                         KERR_TIMEOUT_MMA))
-            return false;
+          const uint32_t pbar = BAR(p_full[0]) + 8 * (2 * (q * S_BUFS + pb));
+          const uint32_t pph = (uint32_t)((cnt_pv[q] / S_BUFS) & 1);
+          if (!mbar_poll(pbar, pph, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
           if (i == 0 && jobs_t[q] > 0) {
             if (!mbar_poll(BAR(o_empty[0]) + 8 * q, (jobs_t[q] - 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
               return false;
@@ -488,8 +485,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           const uint32_t tO = tmem + G::O_COL + q * 128;
           const uint64_t vd = vdesc0 + (((uint32_t)st * G::KV_TILE_BYTES) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk)
+          for (int kk = 0; kk < BN / 32; ++kk)
             umma_ts(tO, tP + kk * 8, vd + ((kk * 2048) >> 4), IDESC_PV, (i == 0 && kk == 0) ? 0u : 1u);
+          if (!mbar_poll(pbar + 8, pph, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = BN / 32; kk < BN / 16; ++kk) umma_ts(tO, tP + kk * 8, vd + ((kk * 2048) >> 4), IDESC_PV, 1u);
           umma_commit(BAR(o_full[0]) + 8 * q);
           ++cnt_pv[q];
           if (q == last_active(i)) umma_commit(BAR(v_empty[0]) + 8 * st);
@@ -611,65 +612,80 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         const bool need = (i > 0) && (mt > m_run + 8.0f);
         const float m_new = (i == 0 || need) ? mt : m_run;
         const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        // P = exp2(S * scale - m): scale/shift and row sums on packed fp32 pairs
+        // P = exp2(S * scale - m): scale/shift and row sums on packed fp32
+        // pairs; POLY_PAIRS of every 16 pairs take the FMA-pipe exponential
         const uint64_t sc2 = f2_pack(sl2, sl2);
         const uint64_t nm2 = f2_pack(-m_use, -m_use);
         uint64_t ls2[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) ls2[k] = f2_pack(0.f, 0.f);
+        auto exp_chunk = [&](int c, uint32_t (&pk)[16]) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float a0, a1, p0, p1;
+            f2_unpack(f2_fma(f2_pack(x[c * 32 + 2 * e], x[c * 32 + 2 * e + 1]), sc2, nm2), a0, a1);
+            const bool poly = POLY_PAIRS > 0 && (e % 16) * POLY_PAIRS % 16 >= 16 - POLY_PAIRS;
+            if (poly) {
+              exp2_poly2(a0, a1, p0, p1);
+            } else {
+              p0 = fast_exp2(a0);
+              p1 = fast_exp2(a1);
+            }
+            ls2[e & 3] = f2_add(ls2[e & 3], f2_pack(p0, p1));
+            pk[e] = pack_bf16x2(p0, p1);
+          }
+        };
+        const uint32_t pbar = BAR(p_full[0]) + 8 * (2 * (q * S_BUFS + sb));
         __syncwarp();  // converge before the warp-collective TMEM stores
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t pk[16];
+          exp_chunk(c, pk);
+          if (c == BN / 64) {
+            // Rescale O when the running max grew by more than 2^8 (here, where
+            // half of the S row is already dead, to keep registers low).  The
+            // S_q(i) commit covers every earlier MMA of the issuer, so PV(i-1)
+            // is complete in the single-buffer case; the wait covers
+            // S_BUFS == 2.  The TMEM round trip is warp-collective: lanes that
+            // keep their max scale by 1.
+            if (i > 0 && __any_sync(0xffffffffu, need)) {
+              if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, (cnt - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
+                aborted = true;
+                break;
+              }
+              tc_fence_after();
+              const float alpha = !need ? 1.f : ((m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new));
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            float a0, a1;
-            f2_unpack(f2_fma(f2_pack(x[c * 32 + 2 * e], x[c * 32 + 2 * e + 1]), sc2, nm2), a0, a1);
-            // spread the polynomial pairs evenly over the chunk
-            const bool poly = POLY_PAIRS > 0 && (e % 16) * POLY_PAIRS % 16 >= 16 - POLY_PAIRS;
-            const float p0 = poly ? exp2_poly(a0) : fast_exp2(a0);
-            const float p1 = poly ? exp2_poly(a1) : fast_exp2(a1);
-            ls2[e & 3] = f2_add(ls2[e & 3], f2_pack(p0, p1));
-            pk[e] = pack_bf16x2(p0, p1);
+              for (int c2 = 0; c2 < HD / 32; ++c2) {
+                float o[32];
+                tmem_ld32f(tO + c2 * 32, o);
+                tmem_wait_ld();
+                uint32_t u[32];
+#pragma unroll
+                for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(o[e] * alpha);
+                tmem_st32(tO + c2 * 32, u);
+              }
+              if (need) l_run *= alpha;
+            }
+            // the first half of P (keys [0, BN/2)) is in TMEM: release it
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(pbar);
           }
           tmem_st16(tS + c * 16, pk);
         }
-        if (i > 0) {
-          // PV of the previous tile must be complete before O is rescaled or
-          // P is released to the next PV
-          if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, (cnt - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
-            aborted = true;
-            break;
-          }
-          tc_fence_after();
-          // the TMEM round trip is warp-collective: lanes that keep their max scale by 1
-          if (__any_sync(0xffffffffu, need)) {
-            const float alpha = !need ? 1.f : ((m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new));
-#pragma unroll
-            for (int c = 0; c < HD / 32; ++c) {
-              float o[32];
-              tmem_ld32f(tO + c * 32, o);
-              tmem_wait_ld();
-              uint32_t u[32];
-#pragma unroll
-              for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(o[e] * alpha);
-              tmem_st32(tO + c * 32, u);
-            }
-            if (need) l_run *= alpha;
-          }
-        }
+        if (aborted) break;
         m_run = m_new;
         {
-          float l0, l1, l2, l3;
+          float l0, l1;
           f2_unpack(f2_add(f2_add(ls2[0], ls2[1]), f2_add(ls2[2], ls2[3])), l0, l1);
-          (void)l2;
-          (void)l3;
           l_run += l0 + l1;
         }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(BAR(p_full[0]) + 8 * (q * S_BUFS + sb));
+        if (lane == 0) mbar_arrive(pbar + 8);
       }
       if (aborted) break;
       // ---- epilogue: normalise, correct, store ----
