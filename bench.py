@@ -65,6 +65,10 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--op", choices=["prefill", "decode"], default="prefill",
+                    help="decode: HBM throughput of the dense / sparse / one-pass decode kernels")
+    ap.add_argument("--decode-caches", type=int, default=8,
+                    help="distinct KV caches cycled through per decode replay (defeats L2 reuse)")
     return ap.parse_args()
 
 
@@ -264,6 +268,81 @@ def workload_config(args, world):
 
 
 # ---------------------------------------------------------------------------
+# decode (bench.py --op decode)
+# ---------------------------------------------------------------------------
+def run_decode(args, local_rank):
+    """HBM throughput of dta_decode at config-2 shapes (one query row per head,
+    a KV cache of --seq keys).  Bytes per call are the algorithmic K+V bytes
+    read: 2 * Hkv * d * 2 B * keys, with keys = n (dense, and the one-pass
+    dense+sparse anchor step) or sink + window (sparse).  Each timed replay is a
+    CUDA graph of one call per cache over --decode-caches distinct caches whose
+    total size exceeds L2 (the sparse calls additionally see an L2 flush before
+    every replay), timed with CUDA events; value = median over --steps replays."""
+    import torch
+
+    from delta_attention_b200 import ops
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    H, Hkv, d, n = args.heads, args.kv_heads, args.head_dim, args.seq
+    C = max(1, args.decode_caches)
+    gen = torch.Generator(device=dev).manual_seed(7)
+    q = (torch.randn(1, H, 1, d, generator=gen, device=dev) * 0.5).bfloat16()
+    caches = [((torch.randn(1, Hkv, n, d, generator=gen, device=dev) * 0.5).bfloat16(),
+               (torch.randn(1, Hkv, n, d, generator=gen, device=dev) * 0.5).bfloat16()) for _ in range(C)]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    peaks, peaks_src = load_peaks()
+    kw = dict(window=args.window, sink=args.sink, scaling=d ** -0.5)
+    sparse_keys = min(n, args.sink + args.window)
+    modes = {
+        "dense": (dict(want_dense=True, want_sparse=False), n),
+        "sparse": (dict(want_dense=False, want_sparse=True), sparse_keys),
+        "dense+sparse (anchor step)": (dict(want_dense=True, want_sparse=True), n),
+    }
+    results = {}
+    sampler = ClockSampler(physical_gpu(local_rank), enabled=not args.no_clocks)
+    with sampler:
+        for name, (flags, keys) in modes.items():
+            for _ in range(max(3, args.warmup)):
+                for kc, vc in caches:
+                    ops.decode(q, kc, vc, **kw, **flags)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for kc, vc in caches:
+                    ops.decode(q, kc, vc, **kw, **flags)
+            times = []
+            for _ in range(max(1, args.steps)):
+                if flags.get("want_dense") is False:
+                    flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                g.replay()
+                e1.record()
+                e1.synchronize()
+                times.append(e0.elapsed_time(e1) / C)  # ms per call
+            del g
+            ms = statistics.median(times)
+            nbytes = 2 * Hkv * d * 2 * keys
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            results[name] = {"us_per_call": round(ms * 1e3, 2), "bytes_per_call": nbytes, "GB/s": round(gbs, 1),
+                             "frac": round(gbs / peaks["hbm_gbs"], 4)}
+    line = {
+        "metric": "delta-attn decode HBM GB/s @128K (Llama-3.1-8B shapes, one layer, one token)",
+        "op": "decode", "unit": "GB/s", "value": results["dense"]["GB/s"], "higher_is_better": True,
+        "n_gpus": 1, "steps": args.steps, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config2 decode: 32q/8kv heads, d=128, one query row per head",
+                   "n_keys": n, "window": args.window, "sink": args.sink, "caches_per_replay": C,
+                   "l2": f"{C} caches x {2 * Hkv * n * d * 2 / 1e6:.0f} MB cycled per replay; sparse replays after an L2 flush"},
+        "roofline": {"bound": "hbm", "peak": peaks["hbm_gbs"], "unit": "GB/s", "peak_source": peaks_src},
+        "modes": results,
+        "clocks": sampler.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
 def run_b200(args, rank, world, local_rank):
@@ -437,6 +516,11 @@ def main():
         return 2
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.op == "decode":
+        if world > 1:
+            print(json.dumps({"error": "--op decode runs on one GPU"}), flush=True)
+            return 2
+        return run_decode(args, local_rank)
     if world > 1:
         import datetime
 
