@@ -305,40 +305,66 @@ int dta_rows(const dta_rows_args* a, void* stream_) {
   return DTA_OK;
 }
 
-static int decode_setup(const dta_decode_args* a, dta::DecodeParams* p) {
+// Chunking of one key set (dta::DecodeSet).
+static void decode_chunking(const dta_decode_args* a, int C, bool sparse, bool all_sparse, dta::DecodeSet* S) {
+  const int n = a->n_keys;
+  S->chunk = C;
+  S->sparse = sparse ? 1 : 0;
+  S->n_chunks = (n + C - 1) / C;
+  const int sink_keys = a->sink < n ? a->sink : n;
+  S->n_sink_chunks = (sink_keys + C - 1) / C;
+  int fw = (n - a->window) / C;
+  if (fw < S->n_sink_chunks) fw = S->n_sink_chunks;
+  S->first_window_chunk = fw;
+  if (!sparse || all_sparse) S->n_launched = S->n_chunks;
+  else S->n_launched = S->n_sink_chunks + (S->n_chunks - fw);
+  S->partials = nullptr;
+}
+
+// Dense chunk for `sms` SMs (0: the shortest chunk, whose partials bound the
+// workspace of every other choice).
+static int decode_dense_chunk(const dta_decode_args* a, int sms) {
+  int C = dta::DEC_DENSE_CHUNK_MAX;
+  if (sms <= 0) return dta::DEC_DENSE_CHUNK_MIN;
+  const long long units = (long long)a->batch * a->n_kv_heads;
+  while (C > dta::DEC_DENSE_CHUNK_MIN && units * ((a->n_keys + C - 1) / C) < (long long)sms) C /= 2;
+  return C;
+}
+
+static int decode_setup(const dta_decode_args* a, dta::DecodeParams* p, int sms) {
   if (!a || a->abi_version != DTA_ABI_VERSION) return DTA_ERR_INVALID_ARG;
   if (a->batch <= 0 || a->n_heads <= 0 || a->n_kv_heads <= 0 || a->n_keys <= 0) return DTA_ERR_SHAPE;
   if (a->head_dim != 64 && a->head_dim != 128) return DTA_ERR_HEAD_DIM;
   if (a->n_heads % a->n_kv_heads != 0 || a->n_heads / a->n_kv_heads > 8) return DTA_ERR_SHAPE;
   if (a->window < 0 || a->sink < 0) return DTA_ERR_INVALID_ARG;
   memset(p, 0, sizeof(*p));
-  const int n = a->n_keys, C = dta::DEC_CHUNK;
+  const int n = a->n_keys;
   p->B = a->batch; p->H = a->n_heads; p->Hkv = a->n_kv_heads; p->G = a->n_heads / a->n_kv_heads;
   p->n_keys = n;
   p->scale_log2 = a->scaling * 1.4426950408889634f;
   p->window = a->window; p->sink = a->sink;
   p->all_sparse = (n <= a->sink + a->window) ? 1 : 0;
-  p->want_dense = a->dense_out ? 1 : 0;
-  p->n_chunks = (n + C - 1) / C;
-  const int sink_keys = a->sink < n ? a->sink : n;
-  p->n_sink_chunks = (sink_keys + C - 1) / C;
-  int fw = (n - a->window) / C;
-  if (fw < p->n_sink_chunks) fw = p->n_sink_chunks;
-  p->first_window_chunk = fw;
-  if (p->want_dense || p->all_sparse) p->n_launched = p->n_chunks;
-  else p->n_launched = p->n_sink_chunks + (p->n_chunks - fw);
+  decode_chunking(a, decode_dense_chunk(a, sms), false, p->all_sparse != 0, &p->set[0]);
+  decode_chunking(a, dta::DEC_SPARSE_CHUNK, true, p->all_sparse != 0, &p->set[1]);
   return DTA_OK;
 }
 
+// bytes of one key set's partials
+static size_t decode_set_bytes(const dta_decode_args* a, const dta::DecodeSet& S) {
+  return align_up((size_t)a->batch * a->n_heads * S.n_launched * (4 + a->head_dim) * 4, 256);
+}
+
+// Both key sets' partials, whichever outputs the call asks for, at the
+// shortest dense chunk (an upper bound for the chunk dta_decode picks).
 size_t dta_decode_workspace_size(const dta_decode_args* a) {
   dta::DecodeParams p;
-  if (decode_setup(a, &p) != DTA_OK) return 0;
-  return align_up((size_t)a->batch * a->n_heads * p.n_chunks * (4 + 2 * a->head_dim) * 4, 256);
+  if (decode_setup(a, &p, 0) != DTA_OK) return 0;
+  return decode_set_bytes(a, p.set[0]) + decode_set_bytes(a, p.set[1]);
 }
 
 int dta_decode(const dta_decode_args* a, void* stream_) {
   dta::DecodeParams p;
-  int st = decode_setup(a, &p);
+  int st = decode_setup(a, &p, 0);
   if (st != DTA_OK) return st;
   if (!a->q || !a->k || !a->v || (!a->dense_out && !a->sparse_out)) return DTA_ERR_INVALID_ARG;
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v)) return DTA_ERR_ALIGNMENT;
@@ -352,13 +378,15 @@ int dta_decode(const dta_decode_args* a, void* stream_) {
   if (!a->workspace || a->workspace_bytes < need || !aligned16(a->workspace)) return DTA_ERR_WORKSPACE;
   int sms = 0;
   if ((st = check_device(&sms)) != DTA_OK) return st;
+  if ((st = decode_setup(a, &p, sms)) != DTA_OK) return st;  // chunking for this device
   p.q = reinterpret_cast<const __nv_bfloat16*>(a->q);
   p.q_sb = a->q_stride_b; p.q_sh = a->q_stride_h;
   p.k = reinterpret_cast<const __nv_bfloat16*>(a->k);
   p.k_sb = a->k_stride_b; p.k_sh = a->k_stride_h; p.k_ss = a->k_stride_s;
   p.v = reinterpret_cast<const __nv_bfloat16*>(a->v);
   p.v_sb = a->v_stride_b; p.v_sh = a->v_stride_h; p.v_ss = a->v_stride_s;
-  p.partials = reinterpret_cast<float*>(a->workspace);
+  p.set[0].partials = reinterpret_cast<float*>(a->workspace);
+  p.set[1].partials = reinterpret_cast<float*>(reinterpret_cast<char*>(a->workspace) + decode_set_bytes(a, p.set[0]));
   p.dense_out = reinterpret_cast<__nv_bfloat16*>(a->dense_out);
   p.sparse_out = reinterpret_cast<__nv_bfloat16*>(a->sparse_out);
   cudaError_t e = dta::launch_decode(p, a->head_dim, reinterpret_cast<cudaStream_t>(stream_));

@@ -1,14 +1,15 @@
 // Decode attention on sm_100a: one query row per (batch, head) over a KV cache.
 //
-// Split-K over the cache: CTA (chunk, batch x kv-group) reads its chunk of K
-// and V exactly once with 16-byte-coalesced loads, serving every query head of
-// the GQA group, and writes an unnormalised partial (max, sum, o[d]) for the
-// DENSE key set and, when the chunk touches it, for the SPARSE key set (the
-// first `sink` keys plus the last `window` keys; delta_attention/llama.py:538-550).
+// Split-K over the cache: CTA (chunk, batch x kv-group, key set) streams its
+// chunk of K and V through shared memory once, serves every query head of the
+// GQA group with tensor-core products, and writes an unnormalised partial
+// (max, sum, o[d]) for its key set: DENSE (every key) or SPARSE (the first
+// `sink` keys plus the last `window` keys; delta_attention/llama.py:538-550).
 // A merge kernel combines the partials with the log-sum-exp rule.  An anchor
-// step of delta decode (delta_attention/llama.py:552-634) therefore gets both
-// its dense and its sparse row from one pass over the cache; a non-anchor step
-// launches only the chunks that intersect the sparse key set.
+// step of delta decode (delta_attention/llama.py:552-634) launches both key
+// sets in one grid (the sparse CTAs of chunks outside the sink and window exit
+// at once, the others re-read their chunk from L2); a non-anchor step launches
+// only the chunks that intersect the sparse key set.
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -24,263 +25,259 @@ __device__ __forceinline__ bool dec_sparse_key(const DecodeParams& p, int j) {
   return p.all_sparse || j < p.sink || j >= p.n_keys - p.window;
 }
 
-__device__ __forceinline__ int dec_chunk_of_block(const DecodeParams& p, int x) {
-  if (p.want_dense || p.all_sparse) return x;
-  return x < p.n_sink_chunks ? x : p.first_window_chunk + (x - p.n_sink_chunks);
+__device__ __forceinline__ int dec_chunk_of_block(const DecodeParams& p, const DecodeSet& S, int x) {
+  if (!S.sparse || p.all_sparse) return x;
+  return x < S.n_sink_chunks ? x : S.first_window_chunk + (x - S.n_sink_chunks);
 }
 
-__device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float* f) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    f[2 * e] = __uint_as_float(w[e] << 16);
-    f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
-  }
+
+// ---------------------------------------------------------------------------
+// Tensor-core partial kernel.  CTA = (chunk of S.chunk keys, batch x KV
+// group, key set), 4 warps.  The chunk's K and V rows stream through shared
+// memory in 64-key stages (cp.async, 16-byte chunks XOR-swizzled by row so
+// ldmatrix is conflict-free, two stages in flight).  Warp w owns keys
+// [16w, 16w + 16) of every stage and runs, per stage, S = Q K^T and O += P V
+// with mma.sync m16n8k16 (bf16 in, fp32 accumulate): the M = 16 rows are the
+// G <= 8 query heads of the group (rows >= G are zero), N runs over keys for
+// S and over head dims for O, and the S accumulator fragments become the P
+// operand fragments in registers.  An online softmax (running max and sum per
+// head, exact rescale) runs on the fragments; the four warps' states are
+// merged once per chunk.  `which` selects the key set and its chunking:
+// 0 = dense (every key, long chunks), 1 = sparse (sink + window, short
+// chunks); an anchor step launches both, and the sparse launch re-reads only
+// the few sink and window chunks (from L2).
+// ---------------------------------------------------------------------------
+constexpr int DEC_STAGE = 64;  // keys per shared-memory stage
+#ifndef DTA_DEC_NSTAGE
+#define DTA_DEC_NSTAGE 3
+#endif
+constexpr int DEC_NSTAGE = DTA_DEC_NSTAGE;  // stages in flight
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D = A B + D, m16n8k16, A row-major bf16, B column-major bf16, fp32 accumulate.
+// Rows 8..15 of A are zero here, so a1 = a3 = 0.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
-// One CTA per (chunk, batch x KV group), one pass over the chunk: each warp
-// streams its own key steps (KPW keys per step, DEC_U steps per batch of
-// loads, K and V of a batch requested before any arithmetic) and keeps an
-// online softmax -- running max, sum and unnormalised o -- for the dense and
-// the sparse key set.  The four warps' states are merged once at the end.
-constexpr int DEC_U = 2;
-template <int HD, int G>
-__global__ void __launch_bounds__(DEC_THREADS, 3) decode_partial_kernel(const __grid_constant__ DecodeParams p) {
-  constexpr int SUB = HD / 16;   // lanes per key in the QK product (16 dims each)
-  constexpr int KPW = 32 / SUB;  // keys per warp step
-  constexpr int DPL = HD / 32;   // dims per lane in the PV product
-  constexpr int NW = DEC_THREADS / 32;
-  __shared__ float wsc[NW][KPW][G];       // one step's scores, broadcast to the warp
-  __shared__ float red_o[NW][G][HD];      // per-warp o, one key set at a time
-  __shared__ float red_ml[NW][4][G];      // per-warp m_d, l_d, m_s, l_s
+template <int HD>
+__global__ void __launch_bounds__(DEC_THREADS) decode_mma_kernel(const __grid_constant__ DecodeParams p, int which) {
+  constexpr int CH = HD / 8;                  // 16-byte chunks per row
+  constexpr int ROWB = HD * 2;                // bytes per K/V row
+  constexpr int STAGE_BYTES = DEC_STAGE * ROWB;
+  constexpr int NT = HD / 8;                  // n-tiles of O
+  extern __shared__ __align__(128) uint8_t dsm[];
+  // layout: [DEC_NSTAGE stages] x {K, V} x STAGE_BYTES; reused for the merge after the loop
+  const uint32_t sbase = smem_u32(dsm);
 
-  const int c = dec_chunk_of_block(p, blockIdx.x);
+  const DecodeSet& S = p.set[which];
+  const int c = dec_chunk_of_block(p, S, blockIdx.x);
   const int bg = blockIdx.y;
   const int b = bg / p.Hkv, g = bg - (bg / p.Hkv) * p.Hkv;
-  const int k0 = c * DEC_CHUNK;
-  const int k1 = min(k0 + DEC_CHUNK, p.n_keys);
+  const int G = p.G;
+  const int k0 = c * S.chunk;
+  const int k1 = min(k0 + S.chunk, p.n_keys);
   const int nk = k1 - k0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int sub = lane % SUB, grp = lane / SUB;
-  const bool chunk_has_sparse = p.all_sparse || k0 < p.sink || k1 > p.n_keys - p.window;
+  const int gr = lane >> 2, cq = lane & 3;  // fragment row (= head) and column pair
+  float* part0 = S.partials + ((long long)(b * p.H + g * G) * S.n_launched + blockIdx.x) * (4 + HD);
+  const long long hstride = (long long)S.n_launched * (4 + HD);
 
-  float qr[G][16];
+  // Q fragments (A operand rows = heads): a0 = q[gr][16kk + 2cq, +1], a2 = [.. + 8]
+  uint32_t qa[HD / 16][2];
+  {
+    const bool hv = gr < G;
+    const __nv_bfloat16* qp = p.q + (long long)b * p.q_sb + (long long)(g * G + (hv ? gr : 0)) * p.q_sh;
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
-    const __nv_bfloat16* qp = p.q + (long long)b * p.q_sb + (long long)(g * G + h) * p.q_sh + sub * 16;
-    bf16x8_to_f32(*reinterpret_cast<const uint4*>(qp), qr[h]);
-    bf16x8_to_f32(*reinterpret_cast<const uint4*>(qp + 8), qr[h] + 8);
-#pragma unroll
-    for (int e = 0; e < 16; ++e) qr[h][e] *= p.scale_log2;
-  }
-  float md[G], ld[G], od[G][DPL], ms[G], ls[G], os[G][DPL];
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    md[h] = ms[h] = -INFINITY;
-    ld[h] = ls[h] = 0.f;
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) od[h][e] = os[h][e] = 0.f;
-  }
-  const __nv_bfloat16* kb = p.k + (long long)b * p.k_sb + (long long)g * p.k_sh + sub * 16;
-  const __nv_bfloat16* vb = p.v + (long long)b * p.v_sb + (long long)g * p.v_sh + lane * DPL;
-  const int n_steps = (nk + KPW - 1) / KPW;
-  // warp-uniform trip count: every lane takes part in every shuffle
-  for (int s0 = warp; s0 < n_steps; s0 += NW * DEC_U) {
-    uint4 kr[DEC_U][2];
-    uint32_t vr[DEC_U][KPW][DPL / 2];
-#pragma unroll
-    for (int u = 0; u < DEC_U; ++u) {
-      const int j0 = (s0 + u * NW) * KPW;  // chunk-local first key of the step
-      const int jk = j0 + grp;
-      const __nv_bfloat16* kp = kb + (long long)(k0 + (jk < nk ? jk : 0)) * p.k_ss;
-      kr[u][0] = *reinterpret_cast<const uint4*>(kp);
-      kr[u][1] = *reinterpret_cast<const uint4*>(kp + 8);
-#pragma unroll
-      for (int kk = 0; kk < KPW; ++kk) {
-        const int jv = j0 + kk;
-        const __nv_bfloat16* vp = vb + (long long)(k0 + (jv < nk ? jv : 0)) * p.v_ss;
-        if constexpr (DPL == 4) {
-          const uint2 w = *reinterpret_cast<const uint2*>(vp);
-          vr[u][kk][0] = w.x;
-          vr[u][kk][1] = w.y;
-        } else {
-          vr[u][kk][0] = *reinterpret_cast<const uint32_t*>(vp);
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < DEC_U; ++u) {
-      const int j0 = (s0 + u * NW) * KPW;
-      if (j0 >= nk) break;  // warp-uniform
-      {
-        float kf[16];
-        bf16x8_to_f32(kr[u][0], kf);
-        bf16x8_to_f32(kr[u][1], kf + 8);
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          float d = 0.f;
-#pragma unroll
-          for (int e = 0; e < 16; ++e) d = fmaf(qr[h][e], kf[e], d);
-#pragma unroll
-          for (int o = SUB / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-          if (sub == 0) wsc[warp][grp][h] = d;
-        }
-      }
-      __syncwarp();
-      float sv[KPW][G];
-#pragma unroll
-      for (int kk = 0; kk < KPW; ++kk)
-#pragma unroll
-        for (int h = 0; h < G; ++h) sv[kk][h] = wsc[warp][kk][h];
-      __syncwarp();
-      float vf[KPW][DPL];
-#pragma unroll
-      for (int kk = 0; kk < KPW; ++kk)
-#pragma unroll
-        for (int e = 0; e < DPL / 2; ++e) {
-          vf[kk][2 * e] = __uint_as_float(vr[u][kk][e] << 16);
-          vf[kk][2 * e + 1] = __uint_as_float(vr[u][kk][e] & 0xffff0000u);
-        }
-      bool live[KPW], spk[KPW];
-#pragma unroll
-      for (int kk = 0; kk < KPW; ++kk) {
-        live[kk] = j0 + kk < nk;
-        spk[kk] = live[kk] && chunk_has_sparse && dec_sparse_key(p, k0 + j0 + kk);
-      }
-      // dense set
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        float mx = md[h];
-#pragma unroll
-        for (int kk = 0; kk < KPW; ++kk) mx = live[kk] ? fmaxf(mx, sv[kk][h]) : mx;
-        const float alpha = (md[h] == -INFINITY) ? 0.f : fast_exp2(md[h] - mx);
-        md[h] = mx;
-        ld[h] *= alpha;
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) od[h][e] *= alpha;
-#pragma unroll
-        for (int kk = 0; kk < KPW; ++kk) {
-          const float pk = live[kk] ? fast_exp2(sv[kk][h] - mx) : 0.f;
-          ld[h] += pk;
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) od[h][e] = fmaf(pk, vf[kk][e], od[h][e]);
-        }
-      }
-      // sparse set (only chunks that touch the sink or the window)
-      if (chunk_has_sparse) {
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          float mx = ms[h];
-#pragma unroll
-          for (int kk = 0; kk < KPW; ++kk) mx = spk[kk] ? fmaxf(mx, sv[kk][h]) : mx;
-          if (mx == -INFINITY) continue;
-          const float alpha = (ms[h] == -INFINITY) ? 0.f : fast_exp2(ms[h] - mx);
-          ms[h] = mx;
-          ls[h] *= alpha;
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) os[h][e] *= alpha;
-#pragma unroll
-          for (int kk = 0; kk < KPW; ++kk) {
-            const float pk = spk[kk] ? fast_exp2(sv[kk][h] - mx) : 0.f;
-            ls[h] += pk;
-#pragma unroll
-            for (int e = 0; e < DPL; ++e) os[h][e] = fmaf(pk, vf[kk][e], os[h][e]);
-          }
-        }
-      }
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      qa[kk][0] = hv ? *reinterpret_cast<const uint32_t*>(qp + kk * 16 + 2 * cq) : 0u;
+      qa[kk][1] = hv ? *reinterpret_cast<const uint32_t*>(qp + kk * 16 + 8 + 2 * cq) : 0u;
     }
   }
-  // ---- merge the warps' states: m = max, l and o rescaled to it ----
-  if (lane == 0) {
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      red_ml[warp][0][h] = md[h];
-      red_ml[warp][1][h] = ld[h];
-      red_ml[warp][2][h] = ms[h];
-      red_ml[warp][3][h] = ls[h];
+  const __nv_bfloat16* kb = p.k + (long long)b * p.k_sb + (long long)g * p.k_sh;
+  const __nv_bfloat16* vb = p.v + (long long)b * p.v_sb + (long long)g * p.v_sh;
+  const int n_stages = (nk + DEC_STAGE - 1) / DEC_STAGE;
+  auto load_stage = [&](int s) {
+    const uint32_t kdst = sbase + (uint32_t)(s % DEC_NSTAGE) * 2 * STAGE_BYTES;
+    const uint32_t vdst = kdst + STAGE_BYTES;
+    const int j0 = s * DEC_STAGE;
+    for (int idx = threadIdx.x; idx < DEC_STAGE * CH; idx += DEC_THREADS) {
+      const int r = idx / CH, ch = idx - (idx / CH) * CH;
+      const int j = j0 + r;
+      const bool ok = j < nk;
+      const long long key = k0 + (ok ? j : 0);
+      const uint32_t off = (uint32_t)(r * ROWB + ((ch ^ (r & 7)) << 4));
+      cp_async_16(kdst + off, kb + key * p.k_ss + ch * 8, ok ? 16u : 0u);
+      cp_async_16(vdst + off, vb + key * p.v_ss + ch * 8, ok ? 16u : 0u);
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  float m_run = -INFINITY, l_run = 0.f;  // head gr (rows >= G carry nothing)
+  float o[NT][4];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+  const float sl2 = p.scale_log2;
+
+  // DEC_NSTAGE - 1 stages ahead; one commit group per iteration (empty past
+  // the end) keeps "stage s complete" at wait_group DEC_NSTAGE - 1
+  for (int s = 0; s < DEC_NSTAGE - 1; ++s) {
+    if (s < n_stages) load_stage(s);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  for (int s = 0; s < n_stages; ++s) {
+    if (s + DEC_NSTAGE - 1 < n_stages) load_stage(s + DEC_NSTAGE - 1);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group %0;" ::"n"(DEC_NSTAGE - 1) : "memory");
+    __syncthreads();
+    const uint32_t ks = sbase + (uint32_t)(s % DEC_NSTAGE) * 2 * STAGE_BYTES;
+    const uint32_t vs = ks + STAGE_BYTES;
+    const int r0 = warp * 16;  // this warp's first key row in the stage
+    // ---- S = Q K^T for 16 keys (two n-tiles of 8 keys) ----
+    float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    {
+      const int mi = lane >> 3, rr = lane & 7;
+      const int r = r0 + (mi >> 1) * 8 + rr;  // matrices 0,1: keys 0-7; 2,3: keys 8-15
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        const int ch = 2 * kk + (mi & 1);
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4(ks + (uint32_t)(r * ROWB + ((ch ^ (r & 7)) << 4)), b00, b01, b10, b11);
+        mma_16816(sacc[0], qa[kk][0], qa[kk][1], b00, b01);
+        mma_16816(sacc[1], qa[kk][0], qa[kk][1], b10, b11);
+      }
+    }
+    // ---- online softmax on row gr: keys 2cq, 2cq+1 (tile 0) and 8+2cq, 9+2cq (tile 1) ----
+    float sv[4] = {sacc[0][0] * sl2, sacc[0][1] * sl2, sacc[1][0] * sl2, sacc[1][1] * sl2};
+    const int jb = s * DEC_STAGE + r0;  // chunk-local key of fragment column 0
+    const int jk[4] = {jb + 2 * cq, jb + 2 * cq + 1, jb + 8 + 2 * cq, jb + 9 + 2 * cq};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const bool v = jk[e] < nk && (!S.sparse || dec_sparse_key(p, k0 + jk[e]));
+      sv[e] = v ? sv[e] : -INFINITY;
+    }
+    float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+    const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
+    float pv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) pv[e] = fast_exp2(sv[e] - m_use);
+    l_run = l_run * alpha + (pv[0] + pv[1]) + (pv[2] + pv[3]);
+    m_run = m_new;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      o[t][0] *= alpha;
+      o[t][1] *= alpha;
+    }
+    const uint32_t pa0 = pack_bf16x2(pv[0], pv[1]);
+    const uint32_t pa2 = pack_bf16x2(pv[2], pv[3]);
+    // ---- O += P V: B fragments by transposed ldmatrix, two n-tiles per load ----
+    {
+      const int mi = lane >> 3, rr = lane & 7;
+      const int r = r0 + (mi & 1) * 8 + rr;  // matrices 0,2: keys 0-7; 1,3: keys 8-15
+#pragma unroll
+      for (int t = 0; t < NT; t += 2) {
+        const int ch = t + (mi >> 1);
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4_t(vs + (uint32_t)(r * ROWB + ((ch ^ (r & 7)) << 4)), b00, b01, b10, b11);
+        mma_16816(o[t], pa0, pa2, b00, b01);
+        mma_16816(o[t + 1], pa0, pa2, b10, b11);
+      }
+    }
+    __syncthreads();  // the stage may be refilled
+  }
+  // ---- merge the four warps: row sums over the 4 lanes of a row, then over warps ----
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  float* red_o = reinterpret_cast<float*>(dsm);                       // [4][8][HD]
+  float* red_ml = red_o + 4 * 8 * HD;                                 // [4][2][8]
+  if (cq == 0) {
+    red_ml[(warp * 2 + 0) * 8 + gr] = m_run;
+    red_ml[(warp * 2 + 1) * 8 + gr] = l_run;
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    red_o[(warp * 8 + gr) * HD + t * 8 + 2 * cq] = o[t][0];
+    red_o[(warp * 8 + gr) * HD + t * 8 + 2 * cq + 1] = o[t][1];
   }
   __syncthreads();
-  float* part0 = p.partials + ((long long)(b * p.H + g * G) * p.n_chunks + c) * (4 + 2 * HD);
-  const long long hstride = (long long)p.n_chunks * (4 + 2 * HD);
-  for (int which = 0; which < 2; ++which) {
-    if (which == 1 && !chunk_has_sparse) break;  // its sparse m stays -inf: the merge skips it
+  for (int idx = threadIdx.x; idx < G * HD; idx += DEC_THREADS) {
+    const int h = idx / HD, t = idx - (idx / HD) * HD;
+    float M = -INFINITY;
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      float M = -INFINITY;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, red_ml[(w * 2) * 8 + h]);
+    float O = 0.f, L = 0.f;
+    if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < NW; ++w) M = fmaxf(M, red_ml[w][2 * which][h]);
-      const float mine = red_ml[warp][2 * which][h];
-      const float sc = (mine == -INFINITY) ? 0.f : fast_exp2(mine - M);
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) red_o[warp][h][lane * DPL + e] = (which == 0 ? od[h][e] : os[h][e]) * sc;
-    }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < G * HD; idx += DEC_THREADS) {
-      const int h = idx / HD, t = idx - (idx / HD) * HD;
-      float sum = 0.f;
-#pragma unroll
-      for (int w = 0; w < NW; ++w) sum += red_o[w][h][t];
-      float* part = part0 + h * hstride;
-      part[4 + which * HD + t] = sum;
-      if (t == 0) {
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, red_ml[w][2 * which][h]);
-        float L = 0.f;
-        if (M != -INFINITY) {
-#pragma unroll
-          for (int w = 0; w < NW; ++w) {
-            const float m = red_ml[w][2 * which][h];
-            if (m != -INFINITY) L += red_ml[w][2 * which + 1][h] * fast_exp2(m - M);
-          }
-        }
-        part[2 * which] = M;
-        part[2 * which + 1] = L;
-        if (which == 0 && !chunk_has_sparse) {
-          part[2] = -INFINITY;
-          part[3] = 0.f;
-        }
+      for (int w = 0; w < 4; ++w) {
+        const float m = red_ml[(w * 2) * 8 + h];
+        if (m == -INFINITY) continue;
+        const float sc = fast_exp2(m - M);
+        O += red_o[(w * 8 + h) * HD + t] * sc;
+        L += red_ml[(w * 2 + 1) * 8 + h] * sc;
       }
     }
-    __syncthreads();
+    float* part = part0 + h * hstride;
+    part[4 + t] = O;
+    if (t == 0) {
+      part[0] = M;
+      part[1] = L;
+    }
   }
 }
 
-// Merge partials of every chunk that was launched: grid (B*H), block HD.
+// Merge the partials of every launched chunk of a key set: grid (B*H), block HD.
 // Chunk statistics are read in batches of 8 independent loads.
 template <int HD>
 __global__ void decode_merge_kernel(const __grid_constant__ DecodeParams p) {
   const int bh = blockIdx.x;
   const int t = threadIdx.x;
-  const float* base = p.partials + (long long)bh * p.n_chunks * (4 + 2 * HD);
-  for (int which = 0; which < 2; ++which) {
-    __nv_bfloat16* dst = which == 0 ? p.dense_out : p.sparse_out;
+  for (int out = 0; out < 2; ++out) {
+    __nv_bfloat16* dst = out == 0 ? p.dense_out : p.sparse_out;
     if (!dst) continue;
-    const int mo = which == 0 ? 0 : 2;
+    // with n <= sink + window the two key sets coincide: both outputs come
+    // from the sparse set's partials
+    const DecodeSet& S = p.set[(out == 1 || p.all_sparse) ? 1 : 0];
+    const float* base = S.partials + (long long)bh * S.n_launched * (4 + HD);
     float M = -INFINITY;
-    for (int x0 = 0; x0 < p.n_launched; x0 += 8) {
+    for (int x0 = 0; x0 < S.n_launched; x0 += 8) {
       float mv[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int x = x0 + u;
-        mv[u] = x < p.n_launched ? base[(long long)dec_chunk_of_block(p, x) * (4 + 2 * HD) + mo] : -INFINITY;
+        mv[u] = x < S.n_launched ? base[(long long)x * (4 + HD)] : -INFINITY;
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) M = fmaxf(M, mv[u]);
     }
     float L = 0.f, O = 0.f;
     if (M != -INFINITY) {
-      for (int x0 = 0; x0 < p.n_launched; x0 += 8) {
+      for (int x0 = 0; x0 < S.n_launched; x0 += 8) {
         float mv[8], lv[8], ov[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const int x = x0 + u;
-          if (x < p.n_launched) {
-            const float* part = base + (long long)dec_chunk_of_block(p, x) * (4 + 2 * HD);
-            mv[u] = part[mo];
-            lv[u] = part[mo + 1];
-            ov[u] = part[4 + which * HD + t];
+          if (x < S.n_launched) {
+            const float* part = base + (long long)x * (4 + HD);
+            mv[u] = part[0];
+            lv[u] = part[1];
+            ov[u] = part[4 + t];
           } else {
             mv[u] = -INFINITY;
             lv[u] = ov[u] = 0.f;
@@ -301,31 +298,25 @@ __global__ void decode_merge_kernel(const __grid_constant__ DecodeParams p) {
   }
 }
 
-template <int HD, int G>
-static void launch_partial(const DecodeParams& p, dim3 grid, cudaStream_t stream) {
-  decode_partial_kernel<HD, G><<<grid, DEC_THREADS, 0, stream>>>(p);
-}
-
 template <int HD>
-static void launch_hd(const DecodeParams& p, dim3 grid, cudaStream_t stream) {
-  switch (p.G) {
-    case 1: launch_partial<HD, 1>(p, grid, stream); break;
-    case 2: launch_partial<HD, 2>(p, grid, stream); break;
-    case 3: launch_partial<HD, 3>(p, grid, stream); break;
-    case 4: launch_partial<HD, 4>(p, grid, stream); break;
-    case 5: launch_partial<HD, 5>(p, grid, stream); break;
-    case 6: launch_partial<HD, 6>(p, grid, stream); break;
-    case 7: launch_partial<HD, 7>(p, grid, stream); break;
-    default: launch_partial<HD, 8>(p, grid, stream); break;
-  }
+static cudaError_t launch_hd(const DecodeParams& p, cudaStream_t stream) {
+  constexpr int smem = DEC_NSTAGE * 2 * DEC_STAGE * HD * 2;
+  static_assert(smem >= (4 * 8 * HD + 4 * 2 * 8) * 4, "merge buffers fit in the stage buffers");
+  cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  const bool dense_set = p.dense_out && !p.all_sparse;
+  const bool sparse_set = p.sparse_out || p.all_sparse;
+  if (dense_set)
+    decode_mma_kernel<HD><<<dim3(p.set[0].n_launched, p.B * p.Hkv), DEC_THREADS, smem, stream>>>(p, 0);
+  if (sparse_set)
+    decode_mma_kernel<HD><<<dim3(p.set[1].n_launched, p.B * p.Hkv), DEC_THREADS, smem, stream>>>(p, 1);
   decode_merge_kernel<HD><<<p.B * p.H, HD, 0, stream>>>(p);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_decode(const DecodeParams& p, int head_dim, cudaStream_t stream) {
-  dim3 grid(p.n_launched, p.B * p.Hkv);
-  if (head_dim == 128) launch_hd<128>(p, grid, stream);
-  else launch_hd<64>(p, grid, stream);
-  return cudaGetLastError();
+  if (head_dim == 128) return launch_hd<128>(p, stream);
+  return launch_hd<64>(p, stream);
 }
 
 }  // namespace dta

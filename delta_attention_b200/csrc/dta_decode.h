@@ -7,7 +7,33 @@
 
 namespace dta {
 
-constexpr int DEC_CHUNK = 512;  // keys per split-K chunk
+// Keys per split-K chunk.  The dense set uses the longest chunk up to
+// DEC_DENSE_CHUNK_MAX that still gives every SM a CTA (long streams per CTA,
+// few partials), never below DEC_DENSE_CHUNK_MIN; the sparse set uses
+// DEC_SPARSE_CHUNK (the sink and window are spread over more CTAs).  All are
+// multiples of the 64-key shared-memory stage.
+#ifndef DTA_DEC_DENSE_CHUNK
+#define DTA_DEC_DENSE_CHUNK 4096
+#endif
+#ifndef DTA_DEC_SPARSE_CHUNK
+#define DTA_DEC_SPARSE_CHUNK 256
+#endif
+constexpr int DEC_DENSE_CHUNK_MAX = DTA_DEC_DENSE_CHUNK;
+constexpr int DEC_DENSE_CHUNK_MIN = 256;
+constexpr int DEC_SPARSE_CHUNK = DTA_DEC_SPARSE_CHUNK;
+
+// Chunking of one key set.  The sparse set always uses DEC_SPARSE_CHUNK, so a
+// sparse row is bit-identical whether it comes from an anchor step (dense +
+// sparse) or from a non-anchor step (sparse only).
+struct DecodeSet {
+  int chunk;               // keys per chunk
+  int n_chunks;            // chunks covering the cache
+  int n_launched;          // chunks launched (all, or the sink + window chunks)
+  int n_sink_chunks;       // chunks covering [0, sink)
+  int first_window_chunk;  // first chunk touching [n_keys - window, n_keys)
+  int sparse;              // 1: keys outside sink + window are skipped
+  float* partials;         // [B, H, n_launched, 4 + d]: (m, l, -, -, o[d]) per launched chunk
+};
 
 struct DecodeParams {
   const __nv_bfloat16* q;
@@ -19,12 +45,7 @@ struct DecodeParams {
   int B, H, Hkv, G, n_keys;
   float scale_log2;
   int window, sink, all_sparse;
-  int want_dense;
-  int n_chunks;            // chunks covering the cache
-  int n_launched;          // chunks launched (all, or the sparse-set chunks)
-  int n_sink_chunks;       // chunks covering [0, sink)
-  int first_window_chunk;  // first chunk touching [n_keys - window, n_keys)
-  float* partials;         // [B, H, n_chunks, 4 + 2 * d]
+  DecodeSet set[2];        // 0: dense (every key), 1: sparse
   __nv_bfloat16* dense_out;
   __nv_bfloat16* sparse_out;
 };
