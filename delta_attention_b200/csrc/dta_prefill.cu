@@ -17,13 +17,17 @@
 //
 // A job is two 128-row query tiles ("A" and "B"); a tile is R rows x G heads of
 // one KV group (R = 128 / G), so the whole GQA group shares every K/V tile.
-// Three warpgroups (384 threads; every thread stays within the 168-register
-// launch budget, so no register re-split is needed):
-//   warp 0      : producer (job fetch, Q by TMA or cp.async gather, K and V by TMA)
-//   warp 1      : TMEM owner; lane 0 issues every tcgen05.mma and commit
-//   warps 2, 3  : idle
-//   warps 4..7  : softmax + epilogue of tile A, one thread per row (TMEM lane)
-//   warps 8..11 : softmax + epilogue of tile B
+// Four warpgroups (512 threads, launched at 128 registers each and re-split
+// with setmaxnreg: control REGS_CTRL, softmax REGS_SOFTMAX, epilogue REGS_EPI):
+//   warp 0       : producer (job fetch, Q by TMA or cp.async gather, K and V by TMA)
+//   warp 1       : TMEM owner; lane 0 issues every tcgen05.mma and commit
+//   warps 2, 3   : idle
+//   warps 4..7   : softmax of tile A, one thread per row (TMEM lane)
+//   warps 8..11  : softmax of tile B
+//   warps 12..15 : epilogue of both tiles: reads O as soon as a job's last PV is
+//                  done, hands the accumulator back to the MMA issuer, then
+//                  normalises, corrects and stores while the softmax warps
+//                  already work on the next job
 // With 128-key tiles each query tile has one S buffer in TMEM and the MMA
 // issue order per key tile i is PV_A(i), S_A(i+1), PV_B(i), S_B(i+1), so the
 // softmax of one query tile overlaps the matrix products of the other.  With
@@ -41,14 +45,58 @@
 
 #include "dta_ptx.cuh"
 #include "dta_prefill.h"
+#include "dta_prefill_jobs.cuh"
 
+namespace dta {
+
+// delta[b, a, h, :] = dense_buf - sparse_buf: bf16 for the windowed launch,
+// optionally fp32 for telemetry
+__global__ void anchor_delta_kernel(const float* __restrict__ dense, const float* __restrict__ sparse,
+                                    __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32, long long n4) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(dense)[i];
+    const float4 b = reinterpret_cast<const float4*>(sparse)[i];
+    const float4 d = make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
+    uint2 w;
+    w.x = pack_bf16x2(d.x, d.y);
+    w.y = pack_bf16x2(d.z, d.w);
+    reinterpret_cast<uint2*>(out_bf16)[i] = w;
+    if (out_f32) reinterpret_cast<float4*>(out_f32)[i] = d;
+  }
+}
+
+cudaError_t launch_anchor_delta(const float* dense, const float* sparse, __nv_bfloat16* delta_bf16, float* delta_f32,
+                                long long n, cudaStream_t s) {
+  const long long n4 = n / 4;
+  int blocks = (int)((n4 + 255) / 256);
+  if (blocks > 4096) blocks = 4096;
+  if (blocks < 1) blocks = 1;
+  anchor_delta_kernel<<<blocks, 256, 0, s>>>(dense, sparse, delta_bf16, delta_f32, n4);
+  return cudaGetLastError();
+}
+
+}  // namespace dta
+
+#if DTA_PREFILL_NQ == 2
 namespace dta {
 
 constexpr int BM = 128;
 constexpr int BN = PREFILL_BN;  // keys per tile
 constexpr int S_BUFS = (BN == 64) ? 2 : 1;  // S buffers per query tile
-constexpr int NUM_THREADS = 128 + PREFILL_NQ * 128;
-constexpr int CTRL_BYTES = 1024;
+constexpr int NUM_THREADS = 128 + PREFILL_NQ * 128 + 128;
+constexpr int CTRL_BYTES = 2048;
+#ifndef DTA_REGS_CTRL
+#define DTA_REGS_CTRL 96
+#endif
+#ifndef DTA_REGS_EPI
+#define DTA_REGS_EPI 64
+#endif
+#ifndef DTA_REGS_SOFTMAX
+#define DTA_REGS_SOFTMAX 176
+#endif
+constexpr int REGS_CTRL = DTA_REGS_CTRL, REGS_EPI = DTA_REGS_EPI, REGS_SOFTMAX = DTA_REGS_SOFTMAX;
+static_assert(128 * REGS_CTRL + 128 * REGS_EPI + PREFILL_NQ * 128 * REGS_SOFTMAX <= NUM_THREADS * 128,
+              "register split exceeds the launch budget");
 constexpr int Q_SLOTS = 3;  // rotating Q tile slots: the next job's Q loads overlap this job
 constexpr int NQ = PREFILL_NQ;
 // Element pairs (of the 16 per 32-column chunk) whose exponentials run on the
@@ -82,133 +130,14 @@ struct Ctrl {
   uint64_t k_full[4], k_empty[4], v_full[4], v_empty[4];
   // p_full[2 * (q * S_BUFS + b) + h]: half h of P (keys [h * BN/2, (h+1) * BN/2))
   uint64_t s_full[NQ * S_BUFS], p_full[NQ * S_BUFS * 2], o_full[NQ], o_empty[NQ];
+  uint64_t l_ready[NQ];     // tile q's row sums of the current job are in xl[q]
   uint64_t drain;
   int job[2][8];
   uint32_t tmem_base;
   int abort_flag;
+  float xl[NQ][128];        // row sums handed from the softmax to the epilogue
 };
 static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block too large");
-
-enum JobKind : int { JOB_END = -1, JOB_WINDOW = 0, JOB_DENSE_ROWS = 1, JOB_SPARSE_ROWS = 2 };
-
-struct Job {
-  int kind, b, g, start, count;
-};
-
-// ---------------------------------------------------------------------------
-// row lists, jobs and key-tile plans (identical in every role)
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ int list_q_row(const PrefillParams& p, int i) {
-  if (p.q_rows) return p.q_rows[i];
-  if (i < p.n_anchor) return p.anchors ? p.anchors[i] : i * p.gamma;
-  return p.s_p + (i - p.n_anchor);
-}
-__device__ __forceinline__ int list_kv_limit(const PrefillParams& p, int i) {
-  if (p.kv_limit) return p.kv_limit[i];
-  return list_q_row(p, i);
-}
-
-__device__ Job decode_job(const PrefillParams& p, int j) {
-  Job J;
-  const int JR = NQ * p.R;  // rows per job
-  if (j >= p.n_jobs) {
-    J.kind = JOB_END;
-    J.b = J.g = J.start = J.count = 0;
-    return J;
-  }
-  if (p.launch == LAUNCH_WINDOW) {
-    const int nt = p.n_window_tiles;
-    const int bg = j / nt, t = j - bg * nt;
-    J.kind = JOB_WINDOW;
-    J.b = bg / p.Hkv;
-    J.g = bg - J.b * p.Hkv;
-    J.start = t * JR;
-    J.count = min(JR, p.row_end - J.start);
-    return J;
-  }
-  const int BG = p.B * p.Hkv;
-  const int rank = j / BG, bg = j - (j / BG) * BG;
-  J.b = bg / p.Hkv;
-  J.g = bg - J.b * p.Hkv;
-  if (rank < p.n_dense_tiles) {
-    const int tile = p.n_dense_tiles - 1 - rank;  // longest (latest rows) first
-    J.kind = JOB_DENSE_ROWS;
-    J.start = tile * JR;
-    J.count = min(JR, p.n_sel - J.start);
-  } else {
-    const int tile = rank - p.n_dense_tiles;
-    J.kind = JOB_SPARSE_ROWS;
-    J.start = tile * JR;
-    J.count = min(JR, p.n_anchor - J.start);
-  }
-  return J;
-}
-
-// position (key limit) of job-local row r (< J.count)
-__device__ __forceinline__ int job_row_pos(const PrefillParams& p, const Job& J, int r) {
-  if (J.kind == JOB_WINDOW) return J.start + r;
-  return list_kv_limit(p, J.start + r);
-}
-
-__device__ __forceinline__ int block_window_lo(const PrefillParams& p, int t) {
-  const int bl = (t / p.qblock) * p.qblock + p.qblock - 1;
-  return max(0, bl - p.window + 1);
-}
-
-// Key tiles of a job: sink segment [0, sink_end) then window segment
-// [lo_min, qmax]; dense jobs have only [0, qmax].  Query tile q takes the
-// prefix of tiles whose first key is <= the tile's last row.
-struct Plan {
-  int n0, n_tiles, sink_end, lo_min, qmax;
-  int qmin_t[NQ], qmax_t[NQ], lo_max_t[NQ], tiles_t[NQ];
-};
-
-__device__ __forceinline__ int tile_key_start(const Plan& P, int i) {
-  return i < P.n0 ? i * BN : P.lo_min + (i - P.n0) * BN;
-}
-
-__device__ Plan make_plan(const PrefillParams& p, const Job& J) {
-  Plan P;
-  const bool dense = (J.kind == JOB_DENSE_ROWS);
-  int first = -1;
-  P.qmax = 0;
-#pragma unroll
-  for (int q = 0; q < NQ; ++q) {
-    const int r0 = q * p.R;
-    const int r1 = min(J.count, (q + 1) * p.R) - 1;
-    if (r1 < r0) {
-      P.qmin_t[q] = 0;
-      P.qmax_t[q] = -1;
-      P.lo_max_t[q] = 0;
-      continue;
-    }
-    P.qmin_t[q] = job_row_pos(p, J, r0);
-    P.qmax_t[q] = job_row_pos(p, J, r1);
-    P.lo_max_t[q] = dense ? 0 : block_window_lo(p, P.qmax_t[q]);
-    if (first < 0) first = P.qmin_t[q];
-    P.qmax = max(P.qmax, P.qmax_t[q]);
-  }
-  if (dense) {
-    P.n0 = 0;
-    P.sink_end = 0;
-    P.lo_min = 0;
-    P.n_tiles = P.qmax / BN + 1;
-  } else {
-    P.lo_min = block_window_lo(p, first);
-    P.sink_end = min(p.sink, P.lo_min);
-    P.n0 = (P.sink_end + BN - 1) / BN;
-    P.n_tiles = P.n0 + (P.qmax - P.lo_min) / BN + 1;
-  }
-#pragma unroll
-  for (int q = 0; q < NQ; ++q) {
-    const int m = P.qmax_t[q];
-    if (m < 0) P.tiles_t[q] = 0;
-    else if (dense) P.tiles_t[q] = m / BN + 1;
-    else if (m >= P.lo_min) P.tiles_t[q] = P.n0 + (m - P.lo_min) / BN + 1;
-    else P.tiles_t[q] = min(P.n0, m / BN + 1);
-  }
-  return P;
-}
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -235,7 +164,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(BAR(job_full[0]) + 8 * i, 1);
-      mbar_init(BAR(job_empty[0]) + 8 * i, 1 + 4 * NQ);  // MMA thread + every softmax warp
+      mbar_init(BAR(job_empty[0]) + 8 * i, 1 + 4 * NQ + 4);  // MMA thread + softmax and epilogue warps
     }
     for (int i = 0; i < Q_SLOTS; ++i) {
       mbar_init(BAR(q_full[0]) + 8 * i, 1);
@@ -254,7 +183,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         mbar_init(BAR(p_full[0]) + 8 * (2 * (q * S_BUFS + b) + 1), 4);
       }
       mbar_init(BAR(o_full[0]) + 8 * q, 1);
-      mbar_init(BAR(o_empty[0]) + 8 * q, 4);
+      mbar_init(BAR(o_empty[0]) + 8 * q, 4);  // epilogue warps
+      mbar_init(BAR(l_ready[0]) + 8 * q, 4);  // softmax warps of tile q
     }
     mbar_init(BAR(drain), 1);
     ctrl->abort_flag = 0;
@@ -278,6 +208,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   const uint32_t tmem = ctrl->tmem_base;
 
   if (warp < 4) {
+  regs_release<REGS_CTRL>();
   if (warp == 0) {
     // ======================= producer =======================
     int n = 0;                // K/V tiles issued so far (ring position)
@@ -529,17 +460,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       }
     }
   }
-  } else {
-    // ======================= softmax + epilogue =======================
+  } else if (warp < 4 + 4 * NQ) {
+    regs_acquire<REGS_SOFTMAX>();
+    // ======================= softmax =======================
     const int q = (warp - 4) >> 2;        // query tile of this warpgroup
     const int quarter = warp & 3;         // TMEM lane quarter this warp may access
     const int r = quarter * 32 + lane;    // row of this thread inside its query tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int hh = r / p.R, rr = r - (r / p.R) * p.R;
+    const int rr = r - (r / p.R) * p.R;
     const uint32_t tS0 = tmem + lane_off + G::S_COL + q * S_BUFS * BN;
     const uint32_t tO = tmem + lane_off + G::O_COL + q * 128;
     const float sl2 = p.scale_log2;
-    int cnt = 0;  // S tiles consumed by this warpgroup (= PVs of its query tile)
+    int cnt = 0;        // S tiles consumed by this warpgroup (= PVs of its query tile)
+    int jobs_done = 0;  // jobs in which this query tile was active
     for (int it = 0;; ++it) {
       const int slot = it & 1;
       if (!mbar_wait_warp(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
@@ -688,7 +621,45 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         if (lane == 0) mbar_arrive(pbar + 8);
       }
       if (aborted) break;
-      // ---- epilogue: normalise, correct, store ----
+      // hand this job's row sums to the epilogue; xl[q] is free once the
+      // epilogue has read the previous job's O (and, before that, its sums)
+      if (jobs_done > 0 &&
+          !mbar_wait_warp(BAR(o_empty[0]) + 8 * q, (jobs_done - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX))
+        break;
+      ctrl->xl[q][r] = l_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(l_ready[0]) + 8 * q);
+      ++jobs_done;
+    }
+  } else {
+    regs_release<REGS_EPI>();
+    // ======================= epilogue =======================
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int hh = r / p.R, rr = r - (r / p.R) * p.R;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    int pv_seen[NQ] = {0, 0};  // PVs of tile q in the jobs handled so far
+    int jobs_seen[NQ] = {0, 0};
+    bool stop = false;
+    for (int it = 0; !stop; ++it) {
+      const int slot = it & 1;
+      if (!mbar_wait_warp(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
+      Job J;
+      {
+        const volatile int* src = ctrl->job[slot];
+        J.kind = src[0]; J.b = src[1]; J.g = src[2]; J.start = src[3]; J.count = src[4];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(job_empty[0]) + 8 * slot);
+      if (J.kind == JOB_END) break;
+      const Plan P = make_plan(p, J);
+      for (int q = 0; q < NQ; ++q) {
+        const int T = P.tiles_t[q];
+        if (T == 0) continue;  // this query tile is empty in this job
+        const uint32_t tO = tmem + lane_off + G::O_COL + q * 128;
+        const int li = q * p.R + rr;  // job-local row
+        const bool row_valid = li < J.count;
+        const int qpos = row_valid ? job_row_pos(p, J, li) : P.qmax_t[q];
       const int h = J.g * p.G + hh;
       const int gli = J.start + li;  // list index (row jobs)
       bool store = row_valid;
@@ -741,9 +712,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
 #pragma unroll
         for (int c = 0; c < HD / 8; ++c) dv[c] = reinterpret_cast<const uint4*>(dlt)[c];
       }
-      if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, (cnt - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
+      if (!mbar_wait_warp(BAR(l_ready[0]) + 8 * q, jobs_seen[q] & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
+        stop = true;
+        break;
+      }
+      const float l_tot = ctrl->xl[q][r];
+      ++jobs_seen[q];
+      pv_seen[q] += T;
+      // o_full[q] completes once per PV of tile q; its next PV (the next job's
+      // first) waits for o_empty[q], so the phase of this job's last PV is current
+      if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, (pv_seen[q] - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
+        stop = true;
+        break;
+      }
       tc_fence_after();
-      const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
+      const float inv_l = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
       // TMEM reads are warp-collective: every lane loads, stores are predicated
       __nv_bfloat16* dst_bf = (store && mode_out == 0)
                                   ? p.out + (((long long)J.b * p.out_rows + out_row) * p.H + h) * HD
@@ -758,6 +741,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         __syncwarp();  // stores below are per-lane; converge before the collective load
         tmem_ld32f(tO + c * 32, o);
         tmem_wait_ld();
+        if (c == HD / 32 - 1) {
+          // O is read: the next job's first PV of this tile may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_relaxed(BAR(o_empty[0]) + 8 * q);
+        }
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] *= inv_l;
         if (dst_bf) {
@@ -786,9 +775,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
             *reinterpret_cast<float4*>(dst_f + c * 32 + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_relaxed(BAR(o_empty[0]) + 8 * q);
+      }
     }
   }
 #undef BAR
@@ -799,22 +786,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, Geo<HD>::TMEM_COLS);
-  }
-}
-
-// delta[b, a, h, :] = dense_buf - sparse_buf: bf16 for the windowed launch,
-// optionally fp32 for telemetry
-__global__ void anchor_delta_kernel(const float* __restrict__ dense, const float* __restrict__ sparse,
-                                    __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32, long long n4) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
-    const float4 a = reinterpret_cast<const float4*>(dense)[i];
-    const float4 b = reinterpret_cast<const float4*>(sparse)[i];
-    const float4 d = make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
-    uint2 w;
-    w.x = pack_bf16x2(d.x, d.y);
-    w.y = pack_bf16x2(d.z, d.w);
-    reinterpret_cast<uint2*>(out_bf16)[i] = w;
-    if (out_f32) reinterpret_cast<float4*>(out_f32)[i] = d;
   }
 }
 
@@ -832,14 +803,5 @@ cudaError_t launch_prefill(const PrefillParams& p, int head_dim, int grid, cudaS
   return launch_prefill_hd<64>(p, grid, stream);
 }
 
-cudaError_t launch_anchor_delta(const float* dense, const float* sparse, __nv_bfloat16* delta_bf16, float* delta_f32,
-                                long long n, cudaStream_t s) {
-  const long long n4 = n / 4;
-  int blocks = (int)((n4 + 255) / 256);
-  if (blocks > 4096) blocks = 4096;
-  if (blocks < 1) blocks = 1;
-  anchor_delta_kernel<<<blocks, 256, 0, s>>>(dense, sparse, delta_bf16, delta_f32, n4);
-  return cudaGetLastError();
-}
-
 }  // namespace dta
+#endif  // DTA_PREFILL_NQ == 2

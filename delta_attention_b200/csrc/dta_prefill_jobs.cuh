@@ -1,0 +1,130 @@
+// Jobs and key-tile plans of the prefill kernels (device code shared by both
+// kernel variants; identical in every role of a kernel).
+#pragma once
+
+#include "dta_prefill.h"
+
+namespace dta {
+
+enum JobKind : int { JOB_END = -1, JOB_WINDOW = 0, JOB_DENSE_ROWS = 1, JOB_SPARSE_ROWS = 2 };
+
+struct Job {
+  int kind, b, g, start, count;
+};
+
+// ---------------------------------------------------------------------------
+// row lists, jobs and key-tile plans (identical in every role)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int list_q_row(const PrefillParams& p, int i) {
+  if (p.q_rows) return p.q_rows[i];
+  if (i < p.n_anchor) return p.anchors ? p.anchors[i] : i * p.gamma;
+  return p.s_p + (i - p.n_anchor);
+}
+__device__ __forceinline__ int list_kv_limit(const PrefillParams& p, int i) {
+  if (p.kv_limit) return p.kv_limit[i];
+  return list_q_row(p, i);
+}
+
+static __device__ Job decode_job(const PrefillParams& p, int j) {
+  Job J;
+  const int JR = PREFILL_NQ * p.R;  // rows per job
+  if (j >= p.n_jobs) {
+    J.kind = JOB_END;
+    J.b = J.g = J.start = J.count = 0;
+    return J;
+  }
+  if (p.launch == LAUNCH_WINDOW) {
+    const int nt = p.n_window_tiles;
+    const int bg = j / nt, t = j - bg * nt;
+    J.kind = JOB_WINDOW;
+    J.b = bg / p.Hkv;
+    J.g = bg - J.b * p.Hkv;
+    J.start = t * JR;
+    J.count = min(JR, p.row_end - J.start);
+    return J;
+  }
+  const int BG = p.B * p.Hkv;
+  const int rank = j / BG, bg = j - (j / BG) * BG;
+  J.b = bg / p.Hkv;
+  J.g = bg - J.b * p.Hkv;
+  if (rank < p.n_dense_tiles) {
+    const int tile = p.n_dense_tiles - 1 - rank;  // longest (latest rows) first
+    J.kind = JOB_DENSE_ROWS;
+    J.start = tile * JR;
+    J.count = min(JR, p.n_sel - J.start);
+  } else {
+    const int tile = rank - p.n_dense_tiles;
+    J.kind = JOB_SPARSE_ROWS;
+    J.start = tile * JR;
+    J.count = min(JR, p.n_anchor - J.start);
+  }
+  return J;
+}
+
+// position (key limit) of job-local row r (< J.count)
+__device__ __forceinline__ int job_row_pos(const PrefillParams& p, const Job& J, int r) {
+  if (J.kind == JOB_WINDOW) return J.start + r;
+  return list_kv_limit(p, J.start + r);
+}
+
+__device__ __forceinline__ int block_window_lo(const PrefillParams& p, int t) {
+  const int bl = (t / p.qblock) * p.qblock + p.qblock - 1;
+  return max(0, bl - p.window + 1);
+}
+
+// Key tiles of a job: sink segment [0, sink_end) then window segment
+// [lo_min, qmax]; dense jobs have only [0, qmax].  Query tile q takes the
+// prefix of tiles whose first key is <= the tile's last row.
+struct Plan {
+  int n0, n_tiles, sink_end, lo_min, qmax;
+  int qmin_t[PREFILL_NQ], qmax_t[PREFILL_NQ], lo_max_t[PREFILL_NQ], tiles_t[PREFILL_NQ];
+};
+
+__device__ __forceinline__ int tile_key_start(const Plan& P, int i) {
+  return i < P.n0 ? i * PREFILL_BN : P.lo_min + (i - P.n0) * PREFILL_BN;
+}
+
+static __device__ Plan make_plan(const PrefillParams& p, const Job& J) {
+  Plan P;
+  const bool dense = (J.kind == JOB_DENSE_ROWS);
+  int first = -1;
+  P.qmax = 0;
+#pragma unroll
+  for (int q = 0; q < PREFILL_NQ; ++q) {
+    const int r0 = q * p.R;
+    const int r1 = min(J.count, (q + 1) * p.R) - 1;
+    if (r1 < r0) {
+      P.qmin_t[q] = 0;
+      P.qmax_t[q] = -1;
+      P.lo_max_t[q] = 0;
+      continue;
+    }
+    P.qmin_t[q] = job_row_pos(p, J, r0);
+    P.qmax_t[q] = job_row_pos(p, J, r1);
+    P.lo_max_t[q] = dense ? 0 : block_window_lo(p, P.qmax_t[q]);
+    if (first < 0) first = P.qmin_t[q];
+    P.qmax = max(P.qmax, P.qmax_t[q]);
+  }
+  if (dense) {
+    P.n0 = 0;
+    P.sink_end = 0;
+    P.lo_min = 0;
+    P.n_tiles = P.qmax / PREFILL_BN + 1;
+  } else {
+    P.lo_min = block_window_lo(p, first);
+    P.sink_end = min(p.sink, P.lo_min);
+    P.n0 = (P.sink_end + PREFILL_BN - 1) / PREFILL_BN;
+    P.n_tiles = P.n0 + (P.qmax - P.lo_min) / PREFILL_BN + 1;
+  }
+#pragma unroll
+  for (int q = 0; q < PREFILL_NQ; ++q) {
+    const int m = P.qmax_t[q];
+    if (m < 0) P.tiles_t[q] = 0;
+    else if (dense) P.tiles_t[q] = m / PREFILL_BN + 1;
+    else if (m >= P.lo_min) P.tiles_t[q] = P.n0 + (m - P.lo_min) / PREFILL_BN + 1;
+    else P.tiles_t[q] = min(P.n0, m / PREFILL_BN + 1);
+  }
+  return P;
+}
+
+}  // namespace dta

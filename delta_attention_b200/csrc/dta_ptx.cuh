@@ -66,7 +66,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+static __device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                             int* err, int code) {
   long long t0 = clock64();
   uint32_t it = 0;
@@ -107,7 +107,7 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-static __device__ __noinline__ bool mbar_poll_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+static __device__ __forceinline__ bool mbar_poll_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                                    int* err, int code) {
   const long long t0 = clock64();
   uint32_t it = 0;
