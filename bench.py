@@ -425,7 +425,10 @@ def run_b200(args, rank, world, local_rank):
     if os.path.exists(tpath):
         with open(tpath) as f:
             tj = json.load(f)
-        if tj.get("seq") == N and tj.get("gamma") == args.gamma:
+        same = (tj.get("seq"), tj.get("gamma"), tj.get("window"), tj.get("sink"), tj.get("heads"),
+                tj.get("kv_heads"), tj.get("head_dim")) == (N, args.gamma, args.window, args.sink, args.heads,
+                                                             args.kv_heads, args.head_dim)
+        if same and (world == 1 or args.scaling == "weak"):  # one whole sequence per rank
             traffic = tj.get("bytes_per_step")
 
     # e2e through the plug-in with pinned host buffers (rank-local units)
