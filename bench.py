@@ -20,7 +20,8 @@ inputs resident in HBM (inputs 1.6 GB per GPU > 126 MB L2, so no L2 flush);
 over the live CUDA-event time of its launches, against MEASURED_PEAKS.json);
 ``e2e`` = the same metric through the reference-facing plug-in
 (``DeltaAttention.delta_forward``) with pinned host inputs, host<->device
-copies inside the timed region; ``cpu_baseline`` = the CPU oracle on a
+copies inside the timed region (consecutive steps overlap their upload,
+compute and download on three streams); ``cpu_baseline`` = the CPU oracle on a
 bounded row sample of the same workload on this host's cores.
 ``--impl reference`` times that CPU implementation as the reference arm.
 """
@@ -60,7 +61,7 @@ def parse_args():
     ap.add_argument("--sink", type=int, default=128)
     ap.add_argument("--gamma", type=int, default=64)
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
@@ -447,26 +448,49 @@ def run_b200(args, rank, world, local_rank):
         mc.num_attention_heads, mc.num_key_value_heads, mc.head_dim = G, 1, d
         plug = DeltaAttention(mc)
         qh, kh, vh = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
-        oh = torch.empty(U, N, G, d, dtype=torch.bfloat16).pin_memory()
-        qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        # Steps are pipelined the way a serving loop overlaps transfers: step i's
+        # host->device copies (copy stream), its plug-in call (compute stream)
+        # and its device->host read of the output (a second copy stream) each
+        # wait only for what they need, with device inputs and host outputs
+        # double-buffered, so step i+1's upload runs during step i's compute.
+        # Every step still moves its own 1.6 GB in and its output out.
+        oh = [torch.empty(U, N, G, d, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        dbuf = [(torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)) for _ in range(2)]
+        s_up, s_comp, s_down = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+        in_ready = [torch.cuda.Event() for _ in range(2)]
+        comp_done = [torch.cuda.Event() for _ in range(2)]
+        used = [False, False]
 
-        def e2e_step():
-            qd.copy_(qh, non_blocking=True)
-            kd.copy_(kh, non_blocking=True)
-            vd.copy_(vh, non_blocking=True)
-            o, _ = plug.delta_forward(plug, qd, kd, vd, None, scaling=d ** -0.5)
-            oh.copy_(o, non_blocking=True)
+        def e2e_step(i):
+            bsl = i & 1
+            qd, kd, vd = dbuf[bsl]
+            if used[bsl]:
+                s_up.wait_event(comp_done[bsl])  # step i-2 has finished reading these inputs
+            with torch.cuda.stream(s_up):
+                qd.copy_(qh, non_blocking=True)
+                kd.copy_(kh, non_blocking=True)
+                vd.copy_(vh, non_blocking=True)
+                in_ready[bsl].record(s_up)
+            s_comp.wait_event(in_ready[bsl])
+            with torch.cuda.stream(s_comp):
+                o, _ = plug.delta_forward(plug, qd, kd, vd, None, scaling=d ** -0.5)
+                comp_done[bsl].record(s_comp)
+            s_down.wait_event(comp_done[bsl])
+            with torch.cuda.stream(s_down):
+                oh[bsl].copy_(o, non_blocking=True)
+            o.record_stream(s_down)
+            used[bsl] = True
 
-        for _ in range(2):
-            e2e_step()
+        for i in range(2):
+            e2e_step(i)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record()
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        s1.record()
+        s0.record(s_up)
+        for i in range(args.e2e_steps):
+            e2e_step(2 + i)
+        s1.record(s_down)  # after the last step's output read, which waited for all of its work
         torch.cuda.synchronize()
         ms_e2e = s0.elapsed_time(s1) / args.e2e_steps
         if world > 1:
@@ -475,9 +499,10 @@ def run_b200(args, rank, world, local_rank):
             ms_e2e = t.item()
         e2e = {"value": tokens_per_step_job / (ms_e2e / 1000.0), "unit": "tokens/s",
                "h2d_bytes_per_step": int(qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2) * world,
-               "d2h_bytes_per_step": int(oh.numel() * 2) * world, "ms_per_step": ms_e2e,
-               "path": "DeltaAttention.delta_forward (plug-in surface) with pinned host q/k/v and output"}
-        del qh, kh, vh, oh, qd, kd, vd
+               "d2h_bytes_per_step": int(oh[0].numel() * 2) * world, "ms_per_step": ms_e2e,
+               "path": "DeltaAttention.delta_forward (plug-in surface) with pinned host q/k/v and output; "
+                       "upload, compute and download of consecutive steps overlap on three streams"}
+        del qh, kh, vh, oh, dbuf
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
