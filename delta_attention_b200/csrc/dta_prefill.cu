@@ -19,7 +19,8 @@
 // one KV group (R = 128 / G), so the whole GQA group shares every K/V tile.
 // Four warpgroups (512 threads, launched at 128 registers each and re-split
 // with setmaxnreg: control REGS_CTRL, softmax REGS_SOFTMAX, epilogue REGS_EPI):
-//   warp 0       : producer (job fetch, Q by TMA or cp.async gather, K and V by TMA)
+//   warp 0       : producer (job fetch, Q by TMA or cp.async gather into two Q
+//                  slots, K by TMA into a 3-stage ring, V into a 2-stage ring)
 //   warp 1       : TMEM owner; lane 0 issues every tcgen05.mma and commit
 //   warps 2, 3   : idle
 //   warps 4..7   : softmax of tile A, one thread per row (TMEM lane)
@@ -97,7 +98,15 @@ constexpr int CTRL_BYTES = 2048;
 constexpr int REGS_CTRL = DTA_REGS_CTRL, REGS_EPI = DTA_REGS_EPI, REGS_SOFTMAX = DTA_REGS_SOFTMAX;
 static_assert(128 * REGS_CTRL + 128 * REGS_EPI + PREFILL_NQ * 128 * REGS_SOFTMAX <= NUM_THREADS * 128,
               "register split exceeds the launch budget");
-constexpr int Q_SLOTS = 3;  // rotating Q tile slots: the next job's Q loads overlap this job
+// Q tile slots: with 2 (the default), tile q keeps slot q; with 3, tile A keeps slot 0 and
+// tile B rotates over the other two, so the next job's Q_B can load while this job still
+// runs.  Measured at config 2: 2 slots and a third K stage 7.63 ms per step, 3 slots and two
+// K stages 8.11 ms.
+#ifndef DTA_Q_SLOTS
+#define DTA_Q_SLOTS 2
+#endif
+constexpr int Q_SLOTS = DTA_Q_SLOTS;
+static_assert(Q_SLOTS == 2 || Q_SLOTS == 3, "Q slots");
 constexpr int NQ = PREFILL_NQ;
 // Element pairs (of the 16 per 32-column chunk) whose exponentials run on the
 // FMA pipe (exp2_poly) instead of the MUFU unit.
@@ -113,11 +122,18 @@ struct Geo {
   static constexpr int TILE_BYTES = REGIONS * REGION_BYTES;  // one 128 x HD bf16 Q tile
   static constexpr int KV_REGION_BYTES = BN * 128;  // K/V: BN rows x 128 bytes
   static constexpr int KV_TILE_BYTES = REGIONS * KV_REGION_BYTES;
-  static constexpr int KV_STAGES = (BN == 64) ? 4 : 2;
+#ifndef DTA_K_STAGES
+#define DTA_K_STAGES 3
+#endif
+#ifndef DTA_V_STAGES
+#define DTA_V_STAGES 2
+#endif
+  static constexpr int K_STAGES = (BN == 64) ? 4 : DTA_K_STAGES;
+  static constexpr int V_STAGES = (BN == 64) ? 4 : DTA_V_STAGES;
   static constexpr int Q_OFF = CTRL_BYTES;
   static constexpr int K_OFF = Q_OFF + Q_SLOTS * TILE_BYTES;
-  static constexpr int V_OFF = K_OFF + KV_STAGES * KV_TILE_BYTES;
-  static constexpr int SMEM_BYTES = V_OFF + KV_STAGES * KV_TILE_BYTES + 1024;  // + alignment slack
+  static constexpr int V_OFF = K_OFF + K_STAGES * KV_TILE_BYTES;
+  static constexpr int SMEM_BYTES = V_OFF + V_STAGES * KV_TILE_BYTES + 1024;  // + alignment slack
   static constexpr int TMEM_COLS = 512;
   static constexpr int S_COL = 0;    // S buffer b of tile q at (q * S_BUFS + b) * BN
   static constexpr int O_COL = 256;  // O of tile q at 256 + q * 128
@@ -170,9 +186,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       mbar_init(BAR(q_full[0]) + 8 * i, 1);
       mbar_init(BAR(q_empty[0]) + 8 * i, 1);
     }
-    for (int i = 0; i < G::KV_STAGES; ++i) {
+    for (int i = 0; i < G::K_STAGES; ++i) {
       mbar_init(BAR(k_full[0]) + 8 * i, 1);
       mbar_init(BAR(k_empty[0]) + 8 * i, 1);
+    }
+    for (int i = 0; i < G::V_STAGES; ++i) {
       mbar_init(BAR(v_full[0]) + 8 * i, 1);
       mbar_init(BAR(v_empty[0]) + 8 * i, 1);
     }
@@ -213,7 +231,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     // ======================= producer =======================
     int n = 0;                // K/V tiles issued so far (ring position)
     int qfree = 1;            // the Q slot tile B takes next (1 or 2)
-    int qfills[Q_SLOTS] = {0, 0, 0};
+    int qfills[3] = {0, 0, 0};
     bool ok = true;
     for (int it = 0; ok; ++it) {
       const int slot = it & 1;
@@ -236,13 +254,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       }
       if (J.kind == JOB_END) break;
       const Plan P = make_plan(p, J);
-      // Q slot rotation (mirrored by the MMA issuer): tile A keeps slot 0, which
-      // the previous job's tile A frees at its last S; tile B takes the free
-      // slot; the previous B slot becomes the free one.  Loads go in the order
-      // Q_B, K0, V0, Q_A, K1, V1, ... so the next job's first tiles are not
-      // queued behind the wait for slot 0.
+      // Q slots (mirrored by the MMA issuer): tile A keeps slot 0, which the
+      // previous job's tile A frees at its last S; tile B takes slot 1 or, with
+      // three slots, the free one (the previous B slot becomes free).  Loads go
+      // in the order Q_B, K0, V0, Q_A, K1, V1, ...
       const int sl[NQ] = {0, qfree};
-      qfree = 3 - qfree;
+      qfree = (Q_SLOTS == 3) ? 3 - qfree : 1;
       auto load_q = [&](int q) -> bool {
         if (P.tiles_t[q] == 0) return true;
         const int qs = sl[q];
@@ -284,8 +301,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       if (!load_q(1)) break;
       // ---- K and V tiles (Q_A after the first pair) ----
       for (int i = 0; i < P.n_tiles; ++i, ++n) {
-        const int st = n % G::KV_STAGES;
-        const uint32_t ph = (uint32_t)((n / G::KV_STAGES) & 1);
+        const int st = n % G::K_STAGES, sv = n % G::V_STAGES;
+        const uint32_t ph = (uint32_t)((n / G::K_STAGES) & 1), phv = (uint32_t)((n / G::V_STAGES) & 1);
         const int ks = tile_key_start(P, i);
         if (!mbar_wait_warp(BAR(k_empty[0]) + 8 * st, ph ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER)) {
           ok = false;
@@ -297,15 +314,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           for (int r = 0; r < G::REGIONS; ++r)
             tma_load_4d(kdst + r * G::KV_REGION_BYTES, &p.tm_k, BAR(k_full[0]) + 8 * st, r * 64, ks, J.g, J.b);
         }
-        if (!mbar_wait_warp(BAR(v_empty[0]) + 8 * st, ph ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER)) {
+        if (!mbar_wait_warp(BAR(v_empty[0]) + 8 * sv, phv ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
         }
         if (lane == 0) {
-          const uint32_t vdst = v_u32 + (uint32_t)st * G::KV_TILE_BYTES;
-          mbar_arrive_expect_tx(BAR(v_full[0]) + 8 * st, G::KV_TILE_BYTES);
+          const uint32_t vdst = v_u32 + (uint32_t)sv * G::KV_TILE_BYTES;
+          mbar_arrive_expect_tx(BAR(v_full[0]) + 8 * sv, G::KV_TILE_BYTES);
           for (int r = 0; r < G::REGIONS; ++r)
-            tma_load_4d(vdst + r * G::KV_REGION_BYTES, &p.tm_v, BAR(v_full[0]) + 8 * st, r * 64, ks, J.g, J.b);
+            tma_load_4d(vdst + r * G::KV_REGION_BYTES, &p.tm_v, BAR(v_full[0]) + 8 * sv, r * 64, ks, J.g, J.b);
         }
         if (i == 0 && !load_q(0)) {
           ok = false;
@@ -315,11 +332,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     }
     // On abort, let in-flight TMA loads land before the CTA can exit.
     if (*abort_flag && lane == 0) {
-      for (int m = max(0, n - G::KV_STAGES); m < n; ++m) {
-        const int st = m % G::KV_STAGES;
-        const uint32_t ph = (uint32_t)((m / G::KV_STAGES) & 1);
+      for (int m = max(0, n - (G::K_STAGES > G::V_STAGES ? G::K_STAGES : G::V_STAGES)); m < n; ++m) {
+        const int st = m % G::K_STAGES, sv = m % G::V_STAGES;
+        const uint32_t ph = (uint32_t)((m / G::K_STAGES) & 1), phv = (uint32_t)((m / G::V_STAGES) & 1);
         const long long t0 = clock64();
-        while (!(mbar_try_wait(BAR(k_full[0]) + 8 * st, ph) && mbar_try_wait(BAR(v_full[0]) + 8 * st, ph))) {
+        while (!(mbar_try_wait(BAR(k_full[0]) + 8 * st, ph) && mbar_try_wait(BAR(v_full[0]) + 8 * sv, phv))) {
           if (clock64() - t0 > kWaitTimeoutCycles) break;
         }
       }
@@ -335,7 +352,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       const uint64_t vdesc0 = smem_desc_sw128(v_u32, G::KV_REGION_BYTES, 1024);
       int n = 0;                // K/V tiles consumed so far (ring position)
       int qfree = 1;            // Q slot of the next job's tile B
-      int quses[Q_SLOTS] = {0, 0, 0};
+      int quses[3] = {0, 0, 0};
       int cnt_s[NQ] = {0, 0};   // S tiles issued per query tile
       int cnt_pv[NQ] = {0, 0};  // PV products issued per query tile
       int jobs_t[NQ] = {0, 0};  // jobs in which query tile q was active
@@ -354,7 +371,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         // Q slots: same rotation as the producer (tile A slot 0, tile B the free slot)
         uint32_t qbuf[NQ];
         int qslot[NQ] = {0, qfree};
-        qfree = 3 - qfree;
+        qfree = (Q_SLOTS == 3) ? 3 - qfree : 1;
         bool qready[NQ] = {false, false};
         for (int q = 0; q < NQ; ++q) qbuf[q] = q_u32 + (uint32_t)qslot[q] * G::TILE_BYTES;
         auto wait_q = [&](int q) -> bool {
@@ -370,10 +387,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         auto last_active = [&](int i) { return (i < P.tiles_t[NQ - 1]) ? NQ - 1 : 0; };
         // S_q(i) = Q_q . K_i^T
         auto issue_s = [&](int q, int i) -> bool {
-          const int m = n0 + i, st = m % G::KV_STAGES;
+          const int m = n0 + i, st = m % G::K_STAGES;
           if (i == 0 && !wait_q(q)) return false;
           if (q == 0 || i >= P.tiles_t[0]) {  // first user of K_i waits for it
-            if (!mbar_poll(BAR(k_full[0]) + 8 * st, (m / G::KV_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+            if (!mbar_poll(BAR(k_full[0]) + 8 * st, (m / G::K_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
               return false;
           }
           tc_fence_after();
@@ -398,7 +415,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         // O_q += P_q(i) . V_i, in two halves of the key tile: the first half
         // of P is released while the softmax still computes the second
         auto issue_pv = [&](int q, int i) -> bool {
-          const int m = n0 + i, st = m % G::KV_STAGES;
+          const int m = n0 + i, st = m % G::V_STAGES;
           const int pb = cnt_pv[q] % S_BUFS;  // S/P buffer of tile i
           const uint32_t pbar = BAR(p_full[0]) + 8 * (2 * (q * S_BUFS + pb));
           const uint32_t pph = (uint32_t)((cnt_pv[q] / S_BUFS) & 1);
@@ -408,7 +425,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
               return false;
           }
           if (q == 0 || i >= P.tiles_t[0]) {  // first user of V_i waits for it
-            if (!mbar_poll(BAR(v_full[0]) + 8 * st, (m / G::KV_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+            if (!mbar_poll(BAR(v_full[0]) + 8 * st, (m / G::V_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
               return false;
           }
           tc_fence_after();
