@@ -37,3 +37,17 @@ def test_decode_dense_and_sparse(n, H, Hkv, d, b, window, sink):
     none, sparse2 = ops.decode(q.cuda(), k.cuda(), v.cuda(), window=window, sink=sink, want_dense=False)
     assert none is None
     assert torch.equal(sparse2, sparse)
+
+
+def test_decode_long_cache_uses_long_chunks():
+    """A 128K-key cache: the dense key set runs in 4096-key chunks (the length
+    the library picks when every SM still gets a CTA) and the sparse set in
+    256-key chunks; both must still match the oracle."""
+    from delta_attention_b200 import ops
+    n, H, Hkv, d, window, sink = 131072, 16, 8, 128, 2048, 128
+    q, k, v = _inputs(n, H, Hkv, d, seed=123)
+    dense, sparse = ops.decode(q.cuda(), k.cuda(), v.cuda(), window=window, sink=sink)
+    sc = d ** -0.5
+    assert_close(dense.cpu(), orc.dense_decode(q.float(), k.float(), v.float(), sc), "dense decode n=131072")
+    assert_close(sparse.cpu(), orc.sparse_decode(q.float(), k.float(), v.float(), window, sink, sc),
+                 "sparse decode n=131072")

@@ -40,6 +40,19 @@ def test_prefill_delta_matches_oracle(s, H, Hkv, d, gamma, window, sink):
     assert_close(out.cpu(), ref, f"delta s={s} H={H}/{Hkv} d={d} g={gamma} W={window} S={sink}")
 
 
+@pytest.mark.parametrize("batch,Hkv", [(2, 2), (3, 1)])
+def test_prefill_batched_sequences(batch, Hkv):
+    """Several sequences in one call: every (sequence, KV group) pair is its own
+    set of jobs (the layout the benchmark uses to stack a rank's units)."""
+    s, d, gamma, window, sink = 768, 128, 64, 192, 64
+    H = 4 * Hkv
+    q, k, v = make_inputs(s, H, Hkv, d, seed=7 + batch, batch=batch)
+    out = _run(q, k, v, gamma=gamma, window=window, sink=sink)
+    torch.cuda.synchronize()
+    ref = _oracle_full(q, k, v, gamma, window, sink)
+    assert_close(out.cpu(), ref, f"batch {batch} Hkv {Hkv}")
+
+
 @pytest.mark.parametrize("mode", ["sparse-only", "recompute"])
 def test_prefill_modes(mode):
     s, H, Hkv, d, gamma, window, sink = 1024, 4, 1, 128, 64, 256, 64
