@@ -43,6 +43,7 @@
 #include <stdint.h>
 #include <cmath>
 #include <cstddef>
+#include <type_traits>
 
 #include "dta_ptx.cuh"
 #include "dta_prefill.h"
@@ -230,8 +231,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   if (warp == 0) {
     // ======================= producer =======================
     int n = 0;                // K/V tiles issued so far (ring position)
-    int qfree = 1;            // the Q slot tile B takes next (1 or 2)
-    int qfills[3] = {0, 0, 0};
+    int q_fills[NQ] = {0, 0};  // Q loads issued per slot (tile q uses slot q)
     bool ok = true;
     for (int it = 0; ok; ++it) {
       const int slot = it & 1;
@@ -254,19 +254,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       }
       if (J.kind == JOB_END) break;
       const Plan P = make_plan(p, J);
-      // Q slots (mirrored by the MMA issuer): tile A keeps slot 0, which the
-      // previous job's tile A frees at its last S; tile B takes slot 1 or, with
-      // three slots, the free one (the previous B slot becomes free).  Loads go
-      // in the order Q_B, K0, V0, Q_A, K1, V1, ...
-      const int sl[NQ] = {0, qfree};
-      qfree = (Q_SLOTS == 3) ? 3 - qfree : 1;
-      auto load_q = [&](int q) -> bool {
+      // Q slots (mirrored by the MMA issuer): tile q keeps slot q, which the
+      // previous job's tile q frees at its last S.  Loads go in the order
+      // Q_B, K0, V0, Q_A, K1, V1, ...  (q is a compile-time constant at
+      // every call, so the per-slot state stays in registers)
+      auto load_q = [&](auto qc) -> bool {
+        constexpr int q = decltype(qc)::value, qs = q;
         if (P.tiles_t[q] == 0) return true;
-        const int qs = sl[q];
         const uint32_t qbuf = q_u32 + (uint32_t)qs * G::TILE_BYTES;
-        if (!mbar_wait_warp(BAR(q_empty[0]) + 8 * qs, (qfills[qs] & 1) ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER))
+        if (!mbar_wait_warp(BAR(q_empty[0]) + 8 * qs, (q_fills[qs] & 1) ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER))
           return false;
-        ++qfills[qs];
+        ++q_fills[qs];
         if (J.kind == JOB_WINDOW) {
           if (lane == 0) {
             mbar_arrive_expect_tx(BAR(q_full[0]) + 8 * qs, G::TILE_BYTES);
@@ -298,7 +296,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         }
         return true;
       };
-      if (!load_q(1)) break;
+      if (!load_q(std::integral_constant<int, 1>{})) break;
       // ---- K and V tiles (Q_A after the first pair) ----
       for (int i = 0; i < P.n_tiles; ++i, ++n) {
         const int st = n % G::K_STAGES, sv = n % G::V_STAGES;
@@ -324,7 +322,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           for (int r = 0; r < G::REGIONS; ++r)
             tma_load_4d(vdst + r * G::KV_REGION_BYTES, &p.tm_v, BAR(v_full[0]) + 8 * sv, r * 64, ks, J.g, J.b);
         }
-        if (i == 0 && !load_q(0)) {
+        if (i == 0 && !load_q(std::integral_constant<int, 0>{})) {
           ok = false;
           break;
         }
@@ -343,19 +341,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     }
   } else if (warp == 1) {
     // ======================= MMA issuer =======================
+    // Per-query-tile state is indexed only by compile-time tile numbers (the
+    // lambdas take std::integral_constant), so it stays in registers: this
+    // thread sits on the S -> softmax -> P -> PV chain and must react to a
+    // released P within a few cycles.
     if (lane == 0) {
+      using QA = std::integral_constant<int, 0>;
+      using QB = std::integral_constant<int, 1>;
       constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, BN, 0);
       constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, HD, 1);
       // base descriptors: Q slot 0 / K stage 0 (K-major), V stage 0 (MN-major)
       const uint64_t qdesc0 = smem_desc_sw128(q_u32, 16, 1024);
       const uint64_t kdesc0 = smem_desc_sw128(k_u32, 16, 1024);
       const uint64_t vdesc0 = smem_desc_sw128(v_u32, G::KV_REGION_BYTES, 1024);
-      int n = 0;                // K/V tiles consumed so far (ring position)
-      int qfree = 1;            // Q slot of the next job's tile B
-      int quses[3] = {0, 0, 0};
-      int cnt_s[NQ] = {0, 0};   // S tiles issued per query tile
-      int cnt_pv[NQ] = {0, 0};  // PV products issued per query tile
-      int jobs_t[NQ] = {0, 0};  // jobs in which query tile q was active
+      int n = 0;                   // K/V tiles consumed so far (ring position)
+      int q_uses[NQ] = {0, 0};     // Q loads consumed per slot (tile q uses slot q)
+      int cnt_pv[NQ] = {0, 0};     // PV products issued per query tile
+      int jobs_t[NQ] = {0, 0};     // jobs in which query tile q was active
       bool aborted = false;
       for (int it = 0; !aborted; ++it) {
         const int slot = it & 1;
@@ -368,37 +370,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         mbar_arrive(BAR(job_empty[0]) + 8 * slot);
         if (J.kind == JOB_END) break;
         const Plan P = make_plan(p, J);
-        // Q slots: same rotation as the producer (tile A slot 0, tile B the free slot)
-        uint32_t qbuf[NQ];
-        int qslot[NQ] = {0, qfree};
-        qfree = (Q_SLOTS == 3) ? 3 - qfree : 1;
-        bool qready[NQ] = {false, false};
-        for (int q = 0; q < NQ; ++q) qbuf[q] = q_u32 + (uint32_t)qslot[q] * G::TILE_BYTES;
-        auto wait_q = [&](int q) -> bool {
-          if (qready[q] || P.tiles_t[q] == 0) return true;
-          const int qs = qslot[q];
-          if (!mbar_poll(BAR(q_full[0]) + 8 * qs, quses[qs] & 1, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
-          ++quses[qs];
-          qready[q] = true;
-          return true;
-        };
+        const int tiles[NQ] = {P.tiles_t[0], P.tiles_t[1]};
         const int n0 = n;  // ring position of this job's key tile 0
-        // the last query tile active at key tile i releases K_i / V_i
-        auto last_active = [&](int i) { return (i < P.tiles_t[NQ - 1]) ? NQ - 1 : 0; };
-        // S_q(i) = Q_q . K_i^T
-        auto issue_s = [&](int q, int i) -> bool {
+        // S_q(i) = Q_q . K_i^T.  K_i is released by the last query tile that uses it.
+        auto issue_s = [&](auto qc, int i) -> bool {
+          constexpr int q = decltype(qc)::value;
           const int m = n0 + i, st = m % G::K_STAGES;
-          if (i == 0 && !wait_q(q)) return false;
-          if (q == 0 || i >= P.tiles_t[0]) {  // first user of K_i waits for it
+          if (i == 0) {
+            if (!mbar_poll(BAR(q_full[0]) + 8 * q, q_uses[q] & 1, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
+            ++q_uses[q];
+          }
+          if (q == 0 || i >= tiles[0]) {  // first user of K_i waits for it
             if (!mbar_poll(BAR(k_full[0]) + 8 * st, (m / G::K_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
               return false;
           }
           tc_fence_after();
-          const int sb = cnt_s[q] % S_BUFS;  // S buffer
-          const uint32_t tS = tmem + G::S_COL + (q * S_BUFS + sb) * BN;
+          const uint32_t tS = tmem + G::S_COL + q * BN;
           // descriptors differ only in the 14-bit start-address field, which
           // never carries out (shared memory < 256 KB), so offsets are plain adds
-          const uint64_t qd = qdesc0 + ((qbuf[q] - q_u32) >> 4);
+          const uint64_t qd = qdesc0 + (((uint32_t)q * G::TILE_BYTES) >> 4);
           const uint64_t kd = kdesc0 + (((uint32_t)st * G::KV_TILE_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
@@ -406,30 +396,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
             const uint32_t koff = ((kk >> 2) * G::KV_REGION_BYTES + (kk & 3) * 32) >> 4;
             umma_ss(tS, qd + qoff, kd + koff, IDESC_QK, kk > 0 ? 1u : 0u);
           }
-          umma_commit(BAR(s_full[0]) + 8 * (q * S_BUFS + sb));
-          ++cnt_s[q];
-          if (q == last_active(i)) umma_commit(BAR(k_empty[0]) + 8 * st);
-          if (i == P.tiles_t[q] - 1) umma_commit(BAR(q_empty[0]) + 8 * qslot[q]);
+          umma_commit(BAR(s_full[0]) + 8 * q);
+          if (q == NQ - 1 || i >= tiles[NQ - 1]) umma_commit(BAR(k_empty[0]) + 8 * st);
+          if (i == tiles[q] - 1) umma_commit(BAR(q_empty[0]) + 8 * q);
           return true;
         };
         // O_q += P_q(i) . V_i, in two halves of the key tile: the first half
         // of P is released while the softmax still computes the second
-        auto issue_pv = [&](int q, int i) -> bool {
+        auto issue_pv = [&](auto qc, int i) -> bool {
+          constexpr int q = decltype(qc)::value;
           const int m = n0 + i, st = m % G::V_STAGES;
-          const int pb = cnt_pv[q] % S_BUFS;  // S/P buffer of tile i
-          const uint32_t pbar = BAR(p_full[0]) + 8 * (2 * (q * S_BUFS + pb));
-          const uint32_t pph = (uint32_t)((cnt_pv[q] / S_BUFS) & 1);
+          const uint32_t pbar = BAR(p_full[0]) + 8 * (2 * q);
+          const uint32_t pph = (uint32_t)(cnt_pv[q] & 1);
           if (!mbar_poll(pbar, pph, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
           if (i == 0 && jobs_t[q] > 0) {
             if (!mbar_poll(BAR(o_empty[0]) + 8 * q, (jobs_t[q] - 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
               return false;
           }
-          if (q == 0 || i >= P.tiles_t[0]) {  // first user of V_i waits for it
+          if (q == 0 || i >= tiles[0]) {  // first user of V_i waits for it
             if (!mbar_poll(BAR(v_full[0]) + 8 * st, (m / G::V_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
               return false;
           }
           tc_fence_after();
-          const uint32_t tP = tmem + G::S_COL + (q * S_BUFS + pb) * BN;
+          const uint32_t tP = tmem + G::S_COL + q * BN;
           const uint32_t tO = tmem + G::O_COL + q * 128;
           const uint64_t vd = vdesc0 + (((uint32_t)st * G::KV_TILE_BYTES) >> 4);
 #pragma unroll
@@ -439,31 +428,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           tc_fence_after();
 #pragma unroll
           for (int kk = BN / 32; kk < BN / 16; ++kk) umma_ts(tO, tP + kk * 8, vd + ((kk * 2048) >> 4), IDESC_PV, 1u);
-          umma_commit(BAR(o_full[0]) + 8 * q);
+          // O of this job is final after its last PV: the epilogue's signal.  (The
+          // softmax needs no per-PV signal: the S_q(i + 1) commit covers PV_q(i).)
+          if (i == tiles[q] - 1) umma_commit(BAR(o_full[0]) + 8 * q);
           ++cnt_pv[q];
-          if (q == last_active(i)) umma_commit(BAR(v_empty[0]) + 8 * st);
+          if (q == NQ - 1 || i >= tiles[NQ - 1]) umma_commit(BAR(v_empty[0]) + 8 * st);
           return true;
         };
-        // prologue: S of the first S_BUFS key tiles for every active query tile
-        for (int i = 0; i < S_BUFS && !aborted; ++i)
-          for (int q = 0; q < NQ && !aborted; ++q)
-            if (i < P.tiles_t[q] && !issue_s(q, i)) aborted = true;
-        for (int i = 0; i < P.n_tiles && !aborted; ++i) {
-          for (int q = 0; q < NQ; ++q) {
-            if (i >= P.tiles_t[q]) continue;
-            if (!issue_pv(q, i)) {
-              aborted = true;
-              break;
-            }
-            if (i + S_BUFS < P.tiles_t[q] && !issue_s(q, i + S_BUFS)) {
-              aborted = true;
-              break;
-            }
+        // prologue: S of key tile 0 for every active query tile; then per key
+        // tile i: PV_A(i), S_A(i+1), PV_B(i), S_B(i+1)
+        if ((tiles[0] > 0 && !issue_s(QA{}, 0)) || (tiles[1] > 0 && !issue_s(QB{}, 0))) break;
+        for (int i = 0; i < P.n_tiles; ++i) {
+          if (i < tiles[0] && (!issue_pv(QA{}, i) || (i + 1 < tiles[0] && !issue_s(QA{}, i + 1)))) {
+            aborted = true;
+            break;
+          }
+          if (i < tiles[1] && (!issue_pv(QB{}, i) || (i + 1 < tiles[1] && !issue_s(QB{}, i + 1)))) {
+            aborted = true;
+            break;
           }
         }
         if (aborted) break;
         for (int q = 0; q < NQ; ++q)
-          if (P.tiles_t[q] > 0) ++jobs_t[q];
+          if (tiles[q] > 0) ++jobs_t[q];
         n += P.n_tiles;
       }
       // drain: every issued tcgen05 op completes before TMEM is released
@@ -502,16 +489,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       if (lane == 0) mbar_arrive(BAR(job_empty[0]) + 8 * slot);
       if (J.kind == JOB_END) break;
       const Plan P = make_plan(p, J);
-      const int T = P.tiles_t[q];
+      // this warpgroup's tile: selects, not a dynamic index, so the plan stays in registers
+      const int T = q ? P.tiles_t[1] : P.tiles_t[0];
       if (T == 0) continue;  // this query tile is empty in this job
       const int li = q * p.R + rr;  // job-local row
       const bool row_valid = li < J.count;
-      const int qpos = row_valid ? job_row_pos(p, J, li) : P.qmax_t[q];
+      const int qpos = row_valid ? job_row_pos(p, J, li) : (q ? P.qmax_t[1] : P.qmax_t[0]);
       const bool sparse_kind = (J.kind != JOB_DENSE_ROWS);
       const int lo_q = sparse_kind ? block_window_lo(p, qpos) : 0;
       const int sink_q = sparse_kind ? p.sink : 0x7fffffff;
-      const int qmin_t = P.qmin_t[q];
-      const int lo_max_t = P.lo_max_t[q];
+      const int qmin_t = q ? P.qmin_t[1] : P.qmin_t[0];
+      const int lo_max_t = q ? P.lo_max_t[1] : P.lo_max_t[0];
 
       float m_run = -INFINITY, l_run = 0.f;
       bool aborted = false;
@@ -595,15 +583,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
             // Rescale O when the running max grew by more than 2^8 (here, where
             // half of the S row is already dead, to keep registers low).  The
             // S_q(i) commit covers every earlier MMA of the issuer, so PV(i-1)
-            // is complete in the single-buffer case; the wait covers
-            // S_BUFS == 2.  The TMEM round trip is warp-collective: lanes that
+            // is complete.  The TMEM round trip is warp-collective: lanes that
             // keep their max scale by 1.
             if (i > 0 && __any_sync(0xffffffffu, need)) {
-              if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, (cnt - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
-                aborted = true;
-                break;
-              }
-              tc_fence_after();
               const float alpha = !need ? 1.f : ((m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new));
 #pragma unroll
               for (int c2 = 0; c2 < HD / 32; ++c2) {
@@ -655,8 +637,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     const int r = quarter * 32 + lane;
     const int hh = r / p.R, rr = r - (r / p.R) * p.R;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    int pv_seen[NQ] = {0, 0};  // PVs of tile q in the jobs handled so far
-    int jobs_seen[NQ] = {0, 0};
+    int jobs_seen[NQ] = {0, 0};  // jobs in which tile q was active
     bool stop = false;
     for (int it = 0; !stop; ++it) {
       const int slot = it & 1;
@@ -685,7 +666,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       const __nv_bfloat16* dlt = nullptr;
       if (J.kind == JOB_WINDOW) {
         out_row = qpos;
-        if (store && p.mode == 0) {
+        // every lane takes its anchor's delta row, rows past the job's end
+        // included (their qpos is the tile's last row), so that the warp can
+        // tell whether all its rows share one
+        if (p.mode == 0 && p.delta_buf) {
           int a;
           if (p.anchors) {
             int lo = 0, hi = p.n_anchor - 1;  // last anchor <= qpos (anchors[0] == 0)
@@ -722,12 +706,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       } else {
         mode_out = 2;
       }
-      // the owning anchor's delta row (bf16) is fetched in one batch of 16-byte
-      // loads before waiting for the last PV, so its latency overlaps that wait
-      uint4 dv[HD / 8];
+      // The owning anchor's delta row (bf16), read chunk by chunk below.  It is
+      // pulled into L1 here, before the waits: a warp's 32 rows are 32
+      // consecutive positions of one head, normally inside one anchor block,
+      // so the per-chunk loads are L1-hit broadcasts.
       if (dlt) {
-#pragma unroll
-        for (int c = 0; c < HD / 8; ++c) dv[c] = reinterpret_cast<const uint4*>(dlt)[c];
+        const char* line = reinterpret_cast<const char*>(dlt) + (lane & (HD * 2 / 128 - 1)) * 128;
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(line));
       }
       if (!mbar_wait_warp(BAR(l_ready[0]) + 8 * q, jobs_seen[q] & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
         stop = true;
@@ -735,15 +720,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       }
       const float l_tot = ctrl->xl[q][r];
       ++jobs_seen[q];
-      pv_seen[q] += T;
-      // o_full[q] completes once per PV of tile q; its next PV (the next job's
-      // first) waits for o_empty[q], so the phase of this job's last PV is current
-      if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, (pv_seen[q] - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
-        stop = true;
-        break;
-      }
-      tc_fence_after();
-      const float inv_l = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
+      // (this warp shares its sub-partitions with two softmax warps and gets
+      // about a third of the issue slots: everything that does not need O is
+      // done before the wait, and the per-element work below is kept short)
+      // 1/l to ~2 ulp (__fdividef): far below the bf16 rounding of the output
+      const float inv_l = (l_tot > 0.f) ? __fdividef(1.f, l_tot) : 0.f;
+      const uint64_t inv2 = f2_pack(inv_l, inv_l);
       // TMEM reads are warp-collective: every lane loads, stores are predicated
       __nv_bfloat16* dst_bf = (store && mode_out == 0)
                                   ? p.out + (((long long)J.b * p.out_rows + out_row) * p.H + h) * HD
@@ -752,11 +734,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
                          ? (mode_out == 1 ? p.dense_buf : p.sparse_buf) +
                                (((long long)J.b * p.n_anchor + gli) * p.H + h) * HD
                          : nullptr;
+      // o_full[q] completes once per job of tile q (after its last PV); the
+      // next job's first PV waits for o_empty[q], so phases cannot run ahead
+      if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, (jobs_seen[q] - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
+        stop = true;
+        break;
+      }
+      tc_fence_after();
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         float o[32];
         __syncwarp();  // stores below are per-lane; converge before the collective load
         tmem_ld32f(tO + c * 32, o);
+        // delta words [16c, 16c + 16) of the row, gathered while the TMEM load runs
+        uint32_t ww[16];
+        if (dlt) {
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            const uint4 w = __ldg(reinterpret_cast<const uint4*>(dlt) + c * 4 + v4);
+            ww[4 * v4] = w.x; ww[4 * v4 + 1] = w.y; ww[4 * v4 + 2] = w.z; ww[4 * v4 + 3] = w.w;
+          }
+        }
         tmem_wait_ld();
         if (c == HD / 32 - 1) {
           // O is read: the next job's first PV of this tile may overwrite it
@@ -764,32 +762,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           __syncwarp();
           if (lane == 0) mbar_arrive_relaxed(BAR(o_empty[0]) + 8 * q);
         }
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] *= inv_l;
         if (dst_bf) {
-          if (dlt) {
-#pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) {
-              const uint4 w = dv[c * 4 + v4];
-              const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                o[v4 * 8 + 2 * k] += __uint_as_float(ww[k] << 16);
-                o[v4 * 8 + 2 * k + 1] += __uint_as_float(ww[k] & 0xffff0000u);
-              }
-            }
-          }
+          // o / l + delta on packed fp32 pairs (one fma.rn.f32x2 per pair)
 #pragma unroll
           for (int e = 0; e < 32; e += 16) {
             uint32_t w[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) w[k] = pack_bf16x2(o[e + 2 * k], o[e + 2 * k + 1]);
+            for (int k = 0; k < 8; ++k) {
+              const int kk = e / 2 + k;
+              const uint64_t d2 = dlt ? f2_pack(__uint_as_float(ww[kk] << 16), __uint_as_float(ww[kk] & 0xffff0000u))
+                                      : f2_pack(0.f, 0.f);
+              float a, b;
+              f2_unpack(f2_fma(f2_pack(o[2 * kk], o[2 * kk + 1]), inv2, d2), a, b);
+              w[k] = pack_bf16x2(a, b);
+            }
             st_global_v8(dst_bf + c * 32 + e, w);
           }
         } else if (dst_f) {
 #pragma unroll
           for (int e = 0; e < 32; e += 4)
-            *reinterpret_cast<float4*>(dst_f + c * 32 + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+            *reinterpret_cast<float4*>(dst_f + c * 32 + e) =
+                make_float4(o[e] * inv_l, o[e + 1] * inv_l, o[e + 2] * inv_l, o[e + 3] * inv_l);
         }
       }
       }
