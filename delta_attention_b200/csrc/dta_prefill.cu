@@ -17,26 +17,22 @@
 //
 // A job is two 128-row query tiles ("A" and "B"); a tile is R rows x G heads of
 // one KV group (R = 128 / G), so the whole GQA group shares every K/V tile.
-// Four warpgroups (512 threads, launched at 128 registers each and re-split
-// with setmaxnreg: control REGS_CTRL, softmax REGS_SOFTMAX, epilogue REGS_EPI):
+// Three warpgroups (384 threads, launched at REGS_LAUNCH registers each and
+// re-split with setmaxnreg: control REGS_CTRL, softmax REGS_SOFTMAX):
 //   warp 0       : producer (job fetch, Q by TMA or cp.async gather into two Q
 //                  slots, K by TMA into a 3-stage ring, V into a 2-stage ring)
 //   warp 1       : TMEM owner; lane 0 issues every tcgen05.mma and commit
 //   warps 2, 3   : idle
-//   warps 4..7   : softmax of tile A, one thread per row (TMEM lane)
-//   warps 8..11  : softmax of tile B
-//   warps 12..15 : epilogue of both tiles: reads O as soon as a job's last PV is
-//                  done, hands the accumulator back to the MMA issuer, then
-//                  normalises, corrects and stores while the softmax warps
-//                  already work on the next job
-// With 128-key tiles each query tile has one S buffer in TMEM and the MMA
-// issue order per key tile i is PV_A(i), S_A(i+1), PV_B(i), S_B(i+1), so the
-// softmax of one query tile overlaps the matrix products of the other.  With
-// 64-key tiles (PREFILL_BN = 64) each query tile has two S buffers and the
-// order is PV_A(i), S_A(i+2), PV_B(i), S_B(i+2).
-// TMEM (512 columns): the S buffers (BN fp32 columns each; P is written back
-// over the first BN/2 columns of its S buffer as packed bf16 and read by the
-// TS-form MMA), then O_A, O_B (head_dim columns each) from column 256.
+//   warps 4..7   : softmax of tile A, one thread per row (TMEM lane); at the end
+//                  of a job the same warps read O, hand the accumulator back to
+//                  the MMA issuer and store the normalised, corrected rows
+//   warps 8..11  : softmax (and epilogue) of tile B
+// Each query tile has one S buffer in TMEM and the MMA issue order per key tile
+// i is PV_A(i), S_A(i+1), PV_B(i), S_B(i+1), so the softmax of one query tile
+// overlaps the matrix products of the other.
+// TMEM (512 columns): S_A, S_B (128 fp32 columns each; P is written back over
+// the first 64 columns of its S buffer as packed bf16 and read by the TS-form
+// MMA), then O_A, O_B (head_dim columns each) from column 256.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -85,19 +81,18 @@ namespace dta {
 constexpr int BM = 128;
 constexpr int BN = PREFILL_BN;  // keys per tile
 constexpr int S_BUFS = (BN == 64) ? 2 : 1;  // S buffers per query tile
-constexpr int NUM_THREADS = 128 + PREFILL_NQ * 128 + 128;
+constexpr int NUM_THREADS = 128 + PREFILL_NQ * 128;
 constexpr int CTRL_BYTES = 2048;
 #ifndef DTA_REGS_CTRL
 #define DTA_REGS_CTRL 96
 #endif
-#ifndef DTA_REGS_EPI
-#define DTA_REGS_EPI 64
-#endif
 #ifndef DTA_REGS_SOFTMAX
-#define DTA_REGS_SOFTMAX 176
+#define DTA_REGS_SOFTMAX 200
 #endif
-constexpr int REGS_CTRL = DTA_REGS_CTRL, REGS_EPI = DTA_REGS_EPI, REGS_SOFTMAX = DTA_REGS_SOFTMAX;
-static_assert(128 * REGS_CTRL + 128 * REGS_EPI + PREFILL_NQ * 128 * REGS_SOFTMAX <= NUM_THREADS * 128,
+// registers per thread at launch (one CTA per SM), rounded down to 8
+constexpr int REGS_LAUNCH = (65536 / NUM_THREADS) & ~7;
+constexpr int REGS_CTRL = DTA_REGS_CTRL, REGS_SOFTMAX = DTA_REGS_SOFTMAX;
+static_assert(128 * REGS_CTRL + PREFILL_NQ * 128 * REGS_SOFTMAX <= NUM_THREADS * REGS_LAUNCH,
               "register split exceeds the launch budget");
 // Q tile slots: with 2 (the default), tile q keeps slot q; with 3, tile A keeps slot 0 and
 // tile B rotates over the other two, so the next job's Q_B can load while this job still
@@ -147,18 +142,21 @@ struct Ctrl {
   uint64_t k_full[4], k_empty[4], v_full[4], v_empty[4];
   // p_full[2 * (q * S_BUFS + b) + h]: half h of P (keys [h * BN/2, (h+1) * BN/2))
   uint64_t s_full[NQ * S_BUFS], p_full[NQ * S_BUFS * 2], o_full[NQ], o_empty[NQ];
-  uint64_t l_ready[NQ];     // tile q's row sums of the current job are in xl[q]
   uint64_t drain;
   int job[2][8];
   uint32_t tmem_base;
   int abort_flag;
-  float xl[NQ][128];        // row sums handed from the softmax to the epilogue
 };
 static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block too large");
 
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
+// bits c >= lo of a 32-bit column word (all for lo <= 0, none for lo >= 32)
+__device__ __forceinline__ uint32_t bits_from(int lo) {
+  return lo <= 0 ? 0xffffffffu : (lo >= 32 ? 0u : (0xffffffffu << lo));
+}
+
 template <int HD>
 __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
   using G = Geo<HD>;
@@ -181,7 +179,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(BAR(job_full[0]) + 8 * i, 1);
-      mbar_init(BAR(job_empty[0]) + 8 * i, 1 + 4 * NQ + 4);  // MMA thread + softmax and epilogue warps
+      mbar_init(BAR(job_empty[0]) + 8 * i, 1 + 4 * NQ);  // MMA thread + softmax warps
     }
     for (int i = 0; i < Q_SLOTS; ++i) {
       mbar_init(BAR(q_full[0]) + 8 * i, 1);
@@ -202,8 +200,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         mbar_init(BAR(p_full[0]) + 8 * (2 * (q * S_BUFS + b) + 1), 4);
       }
       mbar_init(BAR(o_full[0]) + 8 * q, 1);
-      mbar_init(BAR(o_empty[0]) + 8 * q, 4);  // epilogue warps
-      mbar_init(BAR(l_ready[0]) + 8 * q, 4);  // softmax warps of tile q
+      mbar_init(BAR(o_empty[0]) + 8 * q, 4);  // softmax warps of tile q, after reading O
     }
     mbar_init(BAR(drain), 1);
     ctrl->abort_flag = 0;
@@ -499,6 +496,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       const int lo_q = sparse_kind ? block_window_lo(p, qpos) : 0;
       const int sink_q = sparse_kind ? p.sink : 0x7fffffff;
       const int qmin_t = q ? P.qmin_t[1] : P.qmin_t[0];
+      // the owning anchor's delta row (window launch, delta mode), pulled into
+      // L1 now for the epilogue at the end of the job
+      const __nv_bfloat16* dlt = nullptr;
+      if (J.kind == JOB_WINDOW && p.mode == 0 && p.delta_buf) {
+        dlt = p.delta_buf + (((long long)J.b * p.n_anchor + anchor_of(p, qpos)) * p.H + J.g * p.G + r / p.R) * HD;
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char*>(dlt) + (lane & (HD * 2 / 128 - 1)) * 128));
+      }
       const int lo_max_t = q ? P.lo_max_t[1] : P.lo_max_t[0];
 
       float m_run = -INFINITY, l_run = 0.f;
@@ -528,10 +532,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           const int Bq = min(seg_hi - 1, qpos) - ks;
           const int X = sink_q - ks;
           const int Y = lo_q - ks;
+          // as one validity bit per column (32 per word), then one bit test and
+          // one select per element
 #pragma unroll
-          for (int e = 0; e < BN; ++e) {
-            const bool v = (e >= A) && (e <= Bq) && !((e >= X) && (e < Y));
-            x[e] = v ? x[e] : -INFINITY;
+          for (int w = 0; w < BN / 32; ++w) {
+            const int o = 32 * w;
+            const uint32_t m = bits_from(A - o) & ~bits_from(Bq + 1 - o) & ~(bits_from(X - o) & ~bits_from(Y - o));
+#pragma unroll
+            for (int e = 0; e < 32; ++e) x[o + e] = ((m >> e) & 1u) ? x[o + e] : -INFINITY;
           }
         }
         // row max: 8 independent chains of three-input maxima
@@ -620,113 +628,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         if (lane == 0) mbar_arrive(pbar + 8);
       }
       if (aborted) break;
-      // hand this job's row sums to the epilogue; xl[q] is free once the
-      // epilogue has read the previous job's O (and, before that, its sums)
-      if (jobs_done > 0 &&
-          !mbar_wait_warp(BAR(o_empty[0]) + 8 * q, (jobs_done - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX))
-        break;
-      ctrl->xl[q][r] = l_run;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(l_ready[0]) + 8 * q);
-      ++jobs_done;
-    }
-  } else {
-    regs_release<REGS_EPI>();
-    // ======================= epilogue =======================
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
-    const int hh = r / p.R, rr = r - (r / p.R) * p.R;
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    int jobs_seen[NQ] = {0, 0};  // jobs in which tile q was active
-    bool stop = false;
-    for (int it = 0; !stop; ++it) {
-      const int slot = it & 1;
-      if (!mbar_wait_warp(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
-      Job J;
-      {
-        const volatile int* src = ctrl->job[slot];
-        J.kind = src[0]; J.b = src[1]; J.g = src[2]; J.start = src[3]; J.count = src[4];
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(job_empty[0]) + 8 * slot);
-      if (J.kind == JOB_END) break;
-      const Plan P = make_plan(p, J);
-      for (int q = 0; q < NQ; ++q) {
-        const int T = P.tiles_t[q];
-        if (T == 0) continue;  // this query tile is empty in this job
-        const uint32_t tO = tmem + lane_off + G::O_COL + q * 128;
-        const int li = q * p.R + rr;  // job-local row
-        const bool row_valid = li < J.count;
-        const int qpos = row_valid ? job_row_pos(p, J, li) : P.qmax_t[q];
+      // ---- epilogue of this tile: O / l (+ delta) to global memory ----
+      // The destination and the delta row do not depend on O: they are set up
+      // while the last PV runs.  O is read into registers in one batch and
+      // released at once (the next job's first PV of this tile waits for it),
+      // then normalised and stored.
+      const int hh = r / p.R;
       const int h = J.g * p.G + hh;
       const int gli = J.start + li;  // list index (row jobs)
       bool store = row_valid;
       int mode_out = 0;  // 0: bf16 to out, 1: fp32 to dense_buf, 2: fp32 to sparse_buf
       long long out_row = 0;
-      const __nv_bfloat16* dlt = nullptr;
       if (J.kind == JOB_WINDOW) {
         out_row = qpos;
-        // every lane takes its anchor's delta row, rows past the job's end
-        // included (their qpos is the tile's last row), so that the warp can
-        // tell whether all its rows share one
-        if (p.mode == 0 && p.delta_buf) {
-          int a;
-          if (p.anchors) {
-            int lo = 0, hi = p.n_anchor - 1;  // last anchor <= qpos (anchors[0] == 0)
-            while (lo < hi) {
-              const int mid = (lo + hi + 1) >> 1;
-              if (p.anchors[mid] <= qpos) lo = mid; else hi = mid - 1;
-            }
-            a = lo;
-          } else {
-            a = qpos / p.gamma;
-          }
-          dlt = p.delta_buf + (((long long)J.b * p.n_anchor + a) * p.H + h) * HD;
-        } else if (store && p.mode == 1) {
-          bool is_anchor;
-          if (p.anchors) {
-            int lo = 0, hi = p.n_anchor - 1;
-            while (lo < hi) {
-              const int mid = (lo + hi + 1) >> 1;
-              if (p.anchors[mid] <= qpos) lo = mid; else hi = mid - 1;
-            }
-            is_anchor = p.anchors[lo] == qpos;
-          } else {
-            is_anchor = (qpos % p.gamma) == 0;
-          }
-          store = !is_anchor;
+        if (store && p.mode == 1) {
+          store = !is_anchor_row(p, qpos);
         }
       } else if (J.kind == JOB_DENSE_ROWS) {
         if (gli < p.direct_from) {
           mode_out = 1;
         } else {
-          mode_out = 0;
           out_row = !row_valid ? 0 : (p.out_by_list ? gli : list_q_row(p, gli));
         }
       } else {
         mode_out = 2;
       }
-      // The owning anchor's delta row (bf16), read chunk by chunk below.  It is
-      // pulled into L1 here, before the waits: a warp's 32 rows are 32
-      // consecutive positions of one head, normally inside one anchor block,
-      // so the per-chunk loads are L1-hit broadcasts.
-      if (dlt) {
-        const char* line = reinterpret_cast<const char*>(dlt) + (lane & (HD * 2 / 128 - 1)) * 128;
-        asm volatile("prefetch.global.L1 [%0];" ::"l"(line));
-      }
-      if (!mbar_wait_warp(BAR(l_ready[0]) + 8 * q, jobs_seen[q] & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
-        stop = true;
-        break;
-      }
-      const float l_tot = ctrl->xl[q][r];
-      ++jobs_seen[q];
-      // (this warp shares its sub-partitions with two softmax warps and gets
-      // about a third of the issue slots: everything that does not need O is
-      // done before the wait, and the per-element work below is kept short)
       // 1/l to ~2 ulp (__fdividef): far below the bf16 rounding of the output
-      const float inv_l = (l_tot > 0.f) ? __fdividef(1.f, l_tot) : 0.f;
+      const float inv_l = (l_run > 0.f) ? __fdividef(1.f, l_run) : 0.f;
       const uint64_t inv2 = f2_pack(inv_l, inv_l);
-      // TMEM reads are warp-collective: every lane loads, stores are predicated
       __nv_bfloat16* dst_bf = (store && mode_out == 0)
                                   ? p.out + (((long long)J.b * p.out_rows + out_row) * p.H + h) * HD
                                   : nullptr;
@@ -734,57 +663,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
                          ? (mode_out == 1 ? p.dense_buf : p.sparse_buf) +
                                (((long long)J.b * p.n_anchor + gli) * p.H + h) * HD
                          : nullptr;
-      // o_full[q] completes once per job of tile q (after its last PV); the
+      // o_full[q] completes once per job of this tile (after its last PV); the
       // next job's first PV waits for o_empty[q], so phases cannot run ahead
-      if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, (jobs_seen[q] - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
-        stop = true;
-        break;
-      }
+      if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, jobs_done & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
       tc_fence_after();
+      float o[HD];
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        float o[32];
-        __syncwarp();  // stores below are per-lane; converge before the collective load
-        tmem_ld32f(tO + c * 32, o);
-        // delta words [16c, 16c + 16) of the row, gathered while the TMEM load runs
-        uint32_t ww[16];
-        if (dlt) {
+      for (int c = 0; c < HD / 32; ++c) tmem_ld32f(tO + c * 32, o + c * 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(o_empty[0]) + 8 * q);
+      ++jobs_done;
+      if (dst_bf) {
+        // o / l + delta on packed fp32 pairs (one fma.rn.f32x2 per pair); the
+        // delta row is shared by the warp's rows in the common case (L1 hits)
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t ww[16];
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
-            const uint4 w = __ldg(reinterpret_cast<const uint4*>(dlt) + c * 4 + v4);
+            const uint4 w = dlt ? __ldg(reinterpret_cast<const uint4*>(dlt) + c * 4 + v4) : make_uint4(0, 0, 0, 0);
             ww[4 * v4] = w.x; ww[4 * v4 + 1] = w.y; ww[4 * v4 + 2] = w.z; ww[4 * v4 + 3] = w.w;
           }
-        }
-        tmem_wait_ld();
-        if (c == HD / 32 - 1) {
-          // O is read: the next job's first PV of this tile may overwrite it
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_relaxed(BAR(o_empty[0]) + 8 * q);
-        }
-        if (dst_bf) {
-          // o / l + delta on packed fp32 pairs (one fma.rn.f32x2 per pair)
 #pragma unroll
           for (int e = 0; e < 32; e += 16) {
             uint32_t w[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const int kk = e / 2 + k;
-              const uint64_t d2 = dlt ? f2_pack(__uint_as_float(ww[kk] << 16), __uint_as_float(ww[kk] & 0xffff0000u))
-                                      : f2_pack(0.f, 0.f);
+              const uint64_t d2 = f2_pack(__uint_as_float(ww[kk] << 16), __uint_as_float(ww[kk] & 0xffff0000u));
               float a, b;
-              f2_unpack(f2_fma(f2_pack(o[2 * kk], o[2 * kk + 1]), inv2, d2), a, b);
+              f2_unpack(f2_fma(f2_pack(o[c * 32 + 2 * kk], o[c * 32 + 2 * kk + 1]), inv2, d2), a, b);
               w[k] = pack_bf16x2(a, b);
             }
             st_global_v8(dst_bf + c * 32 + e, w);
           }
-        } else if (dst_f) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            *reinterpret_cast<float4*>(dst_f + c * 32 + e) =
-                make_float4(o[e] * inv_l, o[e + 1] * inv_l, o[e + 2] * inv_l, o[e + 3] * inv_l);
         }
-      }
+      } else if (dst_f) {
+#pragma unroll
+        for (int e = 0; e < HD; e += 4)
+          *reinterpret_cast<float4*>(dst_f + e) =
+              make_float4(o[e] * inv_l, o[e + 1] * inv_l, o[e + 2] * inv_l, o[e + 3] * inv_l);
       }
     }
   }

@@ -67,6 +67,21 @@ __device__ __forceinline__ int job_row_pos(const PrefillParams& p, const Job& J,
   return list_kv_limit(p, J.start + r);
 }
 
+// index of the anchor that owns row t: the last anchor row <= t (anchor 0 is row 0)
+__device__ __forceinline__ int anchor_of(const PrefillParams& p, int t) {
+  if (!p.anchors) return t / p.gamma;
+  int lo = 0, hi = p.n_anchor - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.anchors[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+__device__ __forceinline__ bool is_anchor_row(const PrefillParams& p, int t) {
+  if (!p.anchors) return (t % p.gamma) == 0;
+  return p.anchors[anchor_of(p, t)] == t;
+}
+
 __device__ __forceinline__ int block_window_lo(const PrefillParams& p, int t) {
   const int bl = (t / p.qblock) * p.qblock + p.qblock - 1;
   return max(0, bl - p.window + 1);
