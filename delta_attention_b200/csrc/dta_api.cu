@@ -188,6 +188,8 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   p.scale_log2 = a->scaling * 1.4426950408889634f;
   p.window = a->window; p.sink = a->sink; p.qblock = a->q_block;
   p.gamma = a->gamma; p.s_p = L.s_p; p.n_anchor = L.n_anchor; p.n_sel = L.n_sel;
+  dta::fast_div_params(p.qblock, &p.qblock_mul, &p.qblock_sh);
+  if (p.gamma > 0) dta::fast_div_params(p.gamma, &p.gamma_mul, &p.gamma_sh);
   p.anchors = a->anchors;
   p.mode = a->mode;
   p.out_rows = S;
@@ -233,6 +235,10 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   if (phases & DTA_PHASE_WINDOW) {
     dta::PrefillParams w = p;
     w.launch = dta::LAUNCH_WINDOW;
+    // out [B, S, H, d] seen as (d, s, H, B) with a (64, R, G, 1) box: one box is
+    // one query tile, rows in the tile's order (head-major), so full tiles
+    // leave the kernel with a TMA store; without a map the kernel stores rows
+    w.tma_out = encode_4d(&w.tm_out, a->out, d, S, H, B, (long long)H * d, d, (long long)S * H * d, R, G) == DTA_OK;
     w.row_end = (a->mode == DTA_MODE_SPARSE_ONLY) ? S : L.s_p;
     w.n_window_tiles = (w.row_end + JR - 1) / JR;
     w.n_jobs = w.n_window_tiles * B * Hkv;
@@ -279,6 +285,8 @@ int dta_rows(const dta_rows_args* a, void* stream_) {
   p.scale_log2 = a->scaling * 1.4426950408889634f;
   p.window = 0; p.sink = 0; p.qblock = 64;
   p.gamma = 1; p.s_p = 0; p.n_anchor = 0; p.n_sel = a->n_rows;
+  dta::fast_div_params(p.qblock, &p.qblock_mul, &p.qblock_sh);
+  dta::fast_div_params(p.gamma, &p.gamma_mul, &p.gamma_sh);
   p.q_rows = a->q_rows;
   p.kv_limit = a->kv_limit;
   p.mode = DTA_MODE_RECOMPUTE;

@@ -119,7 +119,7 @@ struct Geo {
   static constexpr int KV_REGION_BYTES = BN * 128;  // K/V: BN rows x 128 bytes
   static constexpr int KV_TILE_BYTES = REGIONS * KV_REGION_BYTES;
 #ifndef DTA_K_STAGES
-#define DTA_K_STAGES 3
+#define DTA_K_STAGES 2
 #endif
 #ifndef DTA_V_STAGES
 #define DTA_V_STAGES 2
@@ -129,7 +129,9 @@ struct Geo {
   static constexpr int Q_OFF = CTRL_BYTES;
   static constexpr int K_OFF = Q_OFF + Q_SLOTS * TILE_BYTES;
   static constexpr int V_OFF = K_OFF + K_STAGES * KV_TILE_BYTES;
-  static constexpr int SMEM_BYTES = V_OFF + V_STAGES * KV_TILE_BYTES + 1024;  // + alignment slack
+  // staging tile of the window launch's TMA-store epilogue (one 128-row bf16 tile)
+  static constexpr int STG_OFF = V_OFF + V_STAGES * KV_TILE_BYTES;
+  static constexpr int SMEM_BYTES = STG_OFF + TILE_BYTES + 1024;  // + alignment slack
   static constexpr int TMEM_COLS = 512;
   static constexpr int S_COL = 0;    // S buffer b of tile q at (q * S_BUFS + b) * BN
   static constexpr int O_COL = 256;  // O of tile q at 256 + q * 128
@@ -142,8 +144,11 @@ struct Ctrl {
   uint64_t k_full[4], k_empty[4], v_full[4], v_empty[4];
   // p_full[2 * (q * S_BUFS + b) + h]: half h of P (keys [h * BN/2, (h+1) * BN/2))
   uint64_t s_full[NQ * S_BUFS], p_full[NQ * S_BUFS * 2], o_full[NQ], o_empty[NQ];
+  uint64_t stg_full[NQ];    // tile q's rows are in the staging tile (4 warps)
+  uint64_t stg_free;        // the staging tile's last TMA store has read it
   uint64_t drain;
   int job[2][8];
+  Plan plan[2];             // key-tile plan of job[slot], computed once by the producer
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -202,6 +207,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       mbar_init(BAR(o_full[0]) + 8 * q, 1);
       mbar_init(BAR(o_empty[0]) + 8 * q, 4);  // softmax warps of tile q, after reading O
     }
+    for (int q = 0; q < NQ; ++q) mbar_init(BAR(stg_full[0]) + 8 * q, 4);
+    mbar_init(BAR(stg_free), 1);
     mbar_init(BAR(drain), 1);
     ctrl->abort_flag = 0;
     mbar_init_fence();
@@ -210,6 +217,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
     if (p.launch == LAUNCH_WINDOW) tma_prefetch_desc(&p.tm_q);
+    if (p.tma_out) tma_prefetch_desc(&p.tm_out);
   }
   // Every warp must be converged at a CTA barrier (bar.sync counts whole
   // warps) and at the warp-collective TMEM alloc/dealloc.
@@ -244,13 +252,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
                           KERR_TIMEOUT_PRODUCER))
         break;
       const Job J = decode_job(p, j);
+      // the plan goes out with the job: the consumers would otherwise each
+      // run make_plan, cold code on their critical path at every job change
+      Plan P{};
+      if (J.kind != JOB_END) P = make_plan(p, J);
       if (lane == 0) {
         int* dst = ctrl->job[slot];
         dst[0] = J.kind; dst[1] = J.b; dst[2] = J.g; dst[3] = J.start; dst[4] = J.count;
-        mbar_arrive(BAR(job_full[0]) + 8 * slot);
+        if (J.kind != JOB_END) ctrl->plan[slot] = P;
+        mbar_arrive(BAR(job_full[0]) + 8 * slot);  // release: job and plan are visible to the waiters
       }
       if (J.kind == JOB_END) break;
-      const Plan P = make_plan(p, J);
       // Q slots (mirrored by the MMA issuer): tile q keeps slot q, which the
       // previous job's tile q frees at its last S.  Loads go in the order
       // Q_B, K0, V0, Q_A, K1, V1, ...  (q is a compile-time constant at
@@ -274,9 +286,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           // swizzled K-major layout the MMA expects
           constexpr int CH = HD / 8;  // 16-byte chunks per row
           const __nv_bfloat16* qb = p.q + (long long)J.b * p.q_sb;
+          const int r_shift = __ffs(p.R) - 1;  // R = 128 / G is a power of two
           for (int c = lane; c < BM * CH; c += 32) {
             const int m = c / CH, cc = c - (c / CH) * CH;
-            const int hh = m / p.R, rr = m - (m / p.R) * p.R;
+            const int hh = m >> r_shift, rr = m & (p.R - 1);
             const int li = q * p.R + rr;
             const bool valid = li < J.count;
             const int row = valid ? list_q_row(p, J.start + li) : 0;
@@ -364,9 +377,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           const volatile int* src = ctrl->job[slot];
           J.kind = src[0]; J.b = src[1]; J.g = src[2]; J.start = src[3]; J.count = src[4];
         }
+        const Plan P = ctrl->plan[slot];  // read before the slot is released
         mbar_arrive(BAR(job_empty[0]) + 8 * slot);
         if (J.kind == JOB_END) break;
-        const Plan P = make_plan(p, J);
         const int tiles[NQ] = {P.tiles_t[0], P.tiles_t[1]};
         const int n0 = n;  // ring position of this job's key tile 0
         // S_q(i) = Q_q . K_i^T.  K_i is released by the last query tile that uses it.
@@ -468,12 +481,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     const int quarter = warp & 3;         // TMEM lane quarter this warp may access
     const int r = quarter * 32 + lane;    // row of this thread inside its query tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int rr = r - (r / p.R) * p.R;
+    const int hh = r >> (__ffs(p.R) - 1);  // head of this row inside the KV group (R = 128 / G, a power of two)
+    const int rr = r & (p.R - 1);
     const uint32_t tS0 = tmem + lane_off + G::S_COL + q * S_BUFS * BN;
     const uint32_t tO = tmem + lane_off + G::O_COL + q * 128;
     const float sl2 = p.scale_log2;
     int cnt = 0;        // S tiles consumed by this warpgroup (= PVs of its query tile)
     int jobs_done = 0;  // jobs in which this query tile was active
+    int stg_uses = 0;   // uses of the staging tile by both warpgroups so far
+    int my_stg = 0;     // uses by this warpgroup
     for (int it = 0;; ++it) {
       const int slot = it & 1;
       if (!mbar_wait_warp(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
@@ -482,12 +498,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         const volatile int* src = ctrl->job[slot];
         J.kind = src[0]; J.b = src[1]; J.g = src[2]; J.start = src[3]; J.count = src[4];
       }
+      const Plan P = ctrl->plan[slot];  // read before the slot is released
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(job_empty[0]) + 8 * slot);
       if (J.kind == JOB_END) break;
-      const Plan P = make_plan(p, J);
       // this warpgroup's tile: selects, not a dynamic index, so the plan stays in registers
       const int T = q ? P.tiles_t[1] : P.tiles_t[0];
+      // Window-launch tiles whose 128 rows all lie below row_end leave through
+      // the staging tile and one TMA store (recompute mode skips anchor rows,
+      // so it stores row by row).  Both warpgroups count every use, A before B
+      // within a job, so each knows which release of the staging tile to wait for.
+      const bool stg_ok = p.tma_out && J.kind == JOB_WINDOW && p.mode != 1;
+      const bool stg_a = stg_ok && P.tiles_t[0] > 0 && J.start + p.R <= p.row_end;
+      const bool stg_b = stg_ok && P.tiles_t[1] > 0 && J.start + 2 * p.R <= p.row_end;
+      const bool use_stg = q ? stg_b : stg_a;
+      const int stg_use = stg_uses + ((q == 1 && stg_a) ? 1 : 0);  // index of this tile's use
+      stg_uses += (stg_a ? 1 : 0) + (stg_b ? 1 : 0);
       if (T == 0) continue;  // this query tile is empty in this job
       const int li = q * p.R + rr;  // job-local row
       const bool row_valid = li < J.count;
@@ -500,7 +526,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       // L1 now for the epilogue at the end of the job
       const __nv_bfloat16* dlt = nullptr;
       if (J.kind == JOB_WINDOW && p.mode == 0 && p.delta_buf) {
-        dlt = p.delta_buf + (((long long)J.b * p.n_anchor + anchor_of(p, qpos)) * p.H + J.g * p.G + r / p.R) * HD;
+        dlt = p.delta_buf + (((long long)J.b * p.n_anchor + anchor_of(p, qpos)) * p.H + J.g * p.G + hh) * HD;
         asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char*>(dlt) + (lane & (HD * 2 / 128 - 1)) * 128));
       }
       const int lo_max_t = q ? P.lo_max_t[1] : P.lo_max_t[0];
@@ -633,7 +659,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       // while the last PV runs.  O is read into registers in one batch and
       // released at once (the next job's first PV of this tile waits for it),
       // then normalised and stored.
-      const int hh = r / p.R;
       const int h = J.g * p.G + hh;
       const int gli = J.start + li;  // list index (row jobs)
       bool store = row_valid;
@@ -675,7 +700,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(o_empty[0]) + 8 * q);
       ++jobs_done;
-      if (dst_bf) {
+      if (use_stg) {
+        // the previous user's TMA store must have read the staging tile
+        if (stg_use > 0 && !mbar_wait_warp(BAR(stg_free), (stg_use - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX))
+          break;
+        // row r of the tile (head r / R, position r % R: the order of the
+        // (64, R, G, 1) box) as 128-byte-swizzled 128-byte rows, one region per
+        // 64 columns; o / l + delta on packed fp32 pairs
+        const uint32_t stg = base_u32 + G::STG_OFF;
+#pragma unroll
+        for (int c16 = 0; c16 < HD / 8; ++c16) {
+          const uint4 dv = dlt ? __ldg(reinterpret_cast<const uint4*>(dlt) + c16) : make_uint4(0, 0, 0, 0);
+          const uint32_t dw4[4] = {dv.x, dv.y, dv.z, dv.w};
+          uint32_t w[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int col = c16 * 8 + 2 * k;
+            const uint64_t d2 = f2_pack(__uint_as_float(dw4[k] << 16), __uint_as_float(dw4[k] & 0xffff0000u));
+            float a, b;
+            f2_unpack(f2_fma(f2_pack(o[col], o[col + 1]), inv2, d2), a, b);
+            w[k] = pack_bf16x2(a, b);
+          }
+          const int region = c16 >> 3, cw = c16 & 7;
+          st_shared_v4(stg + region * G::REGION_BYTES + r * 128 + ((cw ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BAR(stg_full[0]) + 8 * q);
+        bool ok = true;
+        if (quarter == 0 && lane == 0) {
+          // leader: once all four warps wrote their rows, store the tile and
+          // release the staging tile when the store has read it
+          ok = mbar_wait(BAR(stg_full[0]) + 8 * q, my_stg & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX);
+          if (ok) {
+            for (int rg = 0; rg < G::REGIONS; ++rg)
+              tma_store_4d(&p.tm_out, stg + rg * G::REGION_BYTES, rg * 64, J.start + q * p.R, J.g * p.G, J.b);
+            bulk_commit_group();
+            bulk_wait_read_all();
+            mbar_arrive(BAR(stg_free));
+          }
+        }
+        if (!__all_sync(0xffffffffu, ok)) break;
+        ++my_stg;
+      } else if (dst_bf) {
         // o / l + delta on packed fp32 pairs (one fma.rn.f32x2 per pair); the
         // delta row is shared by the warp's rows in the common case (L1 hits)
 #pragma unroll
@@ -709,6 +776,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     }
   }
 #undef BAR
+  // bulk (TMA) stores of this thread complete before the CTA exits
+  if (warp >= 4 && (warp & 3) == 0 && lane == 0) bulk_wait_all();
   __syncwarp();
   tc_fence_before();
   __syncthreads();

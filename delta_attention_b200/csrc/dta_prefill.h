@@ -24,12 +24,17 @@ struct PrefillParams {
   CUtensorMap tm_q;  // (d, s, H, B), box (64, R, G, 1): window launch only
   CUtensorMap tm_k;  // (d, s_kv, Hkv, B), box (64, 128, 1, 1)
   CUtensorMap tm_v;
+  CUtensorMap tm_out;  // out (d, s, H, B) with box (64, R, G, 1): window launch, when tma_out
   const __nv_bfloat16* q;
   long long q_sb, q_sh, q_ss;  // element strides for the cp.async row gather
   int B, H, Hkv, G, R;
   float scale_log2;             // scaling * log2(e)
   int window, sink, qblock;
   int gamma, s_p, n_anchor, n_sel;
+  // n / qblock and n / gamma as multiply-shift (fast_div): integer division
+  // would go through the reciprocal unit that the exponentials keep busy
+  unsigned long long qblock_mul, gamma_mul;
+  int qblock_sh, gamma_sh;
   const int* anchors;           // optional explicit anchor rows (sorted)
   const int* q_rows;            // optional explicit row list (rows launch)
   const int* kv_limit;          // optional explicit key limits (rows launch)
@@ -47,7 +52,22 @@ struct PrefillParams {
   float* sparse_buf;            // [B, n_anchor, H, d] fp32
   const __nv_bfloat16* delta_buf;  // [B, n_anchor, H, d] bf16: dense - sparse (window launch)
   __nv_bfloat16* out;           // [B, out_rows, H, d]
+  int tma_out;                  // window launch: full tiles leave through tm_out (TMA stores)
 };
+
+// Multiplier and shift with n / d == (n * mul) >> sh for every 0 <= n < 2^31
+// (Granlund & Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994: mul = ceil(2^(31 + l) / d), l = ceil(log2 d)).
+inline void fast_div_params(int d, unsigned long long* mul, int* sh) {
+  int l = 0;
+  while ((1LL << l) < (long long)d) ++l;
+  const unsigned long long num = 1ULL << (31 + l);
+  *mul = (num + (unsigned long long)d - 1) / (unsigned long long)d;
+  *sh = 31 + l;
+}
+__device__ __forceinline__ int fast_div(int n, unsigned long long mul, int sh) {
+  return (int)(((unsigned long long)(unsigned)n * mul) >> sh);
+}
 
 cudaError_t launch_prefill(const PrefillParams& p, int head_dim, int grid, cudaStream_t stream);
 // delta = dense - sparse per anchor: bf16 into delta_bf16 (for the windowed

@@ -69,7 +69,7 @@ __device__ __forceinline__ int job_row_pos(const PrefillParams& p, const Job& J,
 
 // index of the anchor that owns row t: the last anchor row <= t (anchor 0 is row 0)
 __device__ __forceinline__ int anchor_of(const PrefillParams& p, int t) {
-  if (!p.anchors) return t / p.gamma;
+  if (!p.anchors) return fast_div(t, p.gamma_mul, p.gamma_sh);
   int lo = 0, hi = p.n_anchor - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -78,12 +78,12 @@ __device__ __forceinline__ int anchor_of(const PrefillParams& p, int t) {
   return lo;
 }
 __device__ __forceinline__ bool is_anchor_row(const PrefillParams& p, int t) {
-  if (!p.anchors) return (t % p.gamma) == 0;
+  if (!p.anchors) return t == fast_div(t, p.gamma_mul, p.gamma_sh) * p.gamma;
   return p.anchors[anchor_of(p, t)] == t;
 }
 
 __device__ __forceinline__ int block_window_lo(const PrefillParams& p, int t) {
-  const int bl = (t / p.qblock) * p.qblock + p.qblock - 1;
+  const int bl = fast_div(t, p.qblock_mul, p.qblock_sh) * p.qblock + p.qblock - 1;
   return max(0, bl - p.window + 1);
 }
 

@@ -53,9 +53,12 @@ def test_prefill_batched_sequences(batch, Hkv):
     assert_close(out.cpu(), ref, f"batch {batch} Hkv {Hkv}")
 
 
-@pytest.mark.parametrize("mode", ["sparse-only", "recompute"])
-def test_prefill_modes(mode):
-    s, H, Hkv, d, gamma, window, sink = 1024, 4, 1, 128, 64, 256, 64
+@pytest.mark.parametrize("mode,s", [("sparse-only", 1024), ("recompute", 1024),
+                                    ("sparse-only", 1000), ("recompute", 1000)])
+def test_prefill_modes(mode, s):
+    """s=1000: the last job's second query tile is partial, so one job mixes a
+    tile stored by TMA (sparse-only) with a tile stored row by row."""
+    H, Hkv, d, gamma, window, sink = 4, 1, 128, 8, 256, 64
     q, k, v = make_inputs(s, H, Hkv, d, seed=3)
     out = _run(q, k, v, gamma=gamma, window=window, sink=sink, mode=mode)
     ref = _oracle_full(q, k, v, gamma, window, sink, mode=mode)
