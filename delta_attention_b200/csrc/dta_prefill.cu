@@ -351,11 +351,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     }
   } else if (warp == 1) {
     // ======================= MMA issuer =======================
-    // Per-query-tile state is indexed only by compile-time tile numbers (the
-    // lambdas take std::integral_constant), so it stays in registers: this
-    // thread sits on the S -> softmax -> P -> PV chain and must react to a
-    // released P within a few cycles.
-    if (lane == 0) {
+    // The whole warp runs the issue loop (warp-uniform waits, descriptors and
+    // counters) and one elected lane issues each batch of tcgen05.mma and
+    // commits.  Per-query-tile state is indexed only by compile-time tile
+    // numbers (the lambdas take std::integral_constant), so it stays in
+    // registers: this warp sits on the S -> softmax -> P -> PV chain and must
+    // react to a released P within a few cycles.
+    {
       using QA = std::integral_constant<int, 0>;
       using QB = std::integral_constant<int, 1>;
       constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, BN, 0);
@@ -378,7 +380,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           J.kind = src[0]; J.b = src[1]; J.g = src[2]; J.start = src[3]; J.count = src[4];
         }
         const Plan P = ctrl->plan[slot];  // read before the slot is released
-        mbar_arrive(BAR(job_empty[0]) + 8 * slot);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BAR(job_empty[0]) + 8 * slot);
         if (J.kind == JOB_END) break;
         const int tiles[NQ] = {P.tiles_t[0], P.tiles_t[1]};
         const int n0 = n;  // ring position of this job's key tile 0
@@ -400,15 +403,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           // never carries out (shared memory < 256 KB), so offsets are plain adds
           const uint64_t qd = qdesc0 + (((uint32_t)q * G::TILE_BYTES) >> 4);
           const uint64_t kd = kdesc0 + (((uint32_t)st * G::KV_TILE_BYTES) >> 4);
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t qoff = ((kk >> 2) * G::REGION_BYTES + (kk & 3) * 32) >> 4;
-            const uint32_t koff = ((kk >> 2) * G::KV_REGION_BYTES + (kk & 3) * 32) >> 4;
-            umma_ss(tS, qd + qoff, kd + koff, IDESC_QK, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < HD / 16; ++kk) {
+              const uint32_t qoff = ((kk >> 2) * G::REGION_BYTES + (kk & 3) * 32) >> 4;
+              const uint32_t koff = ((kk >> 2) * G::KV_REGION_BYTES + (kk & 3) * 32) >> 4;
+              umma_ss(tS, qd + qoff, kd + koff, IDESC_QK, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(BAR(s_full[0]) + 8 * q);
+            if (q == NQ - 1 || i >= tiles[NQ - 1]) umma_commit(BAR(k_empty[0]) + 8 * st);
+            if (i == tiles[q] - 1) umma_commit(BAR(q_empty[0]) + 8 * q);
           }
-          umma_commit(BAR(s_full[0]) + 8 * q);
-          if (q == NQ - 1 || i >= tiles[NQ - 1]) umma_commit(BAR(k_empty[0]) + 8 * st);
-          if (i == tiles[q] - 1) umma_commit(BAR(q_empty[0]) + 8 * q);
+          __syncwarp();
           return true;
         };
         // O_q += P_q(i) . V_i, in two halves of the key tile: the first half
@@ -431,18 +437,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           const uint32_t tP = tmem + G::S_COL + q * BN;
           const uint32_t tO = tmem + G::O_COL + q * 128;
           const uint64_t vd = vdesc0 + (((uint32_t)st * G::KV_TILE_BYTES) >> 4);
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < BN / 32; ++kk)
-            umma_ts(tO, tP + kk * 8, vd + ((kk * 2048) >> 4), IDESC_PV, (i == 0 && kk == 0) ? 0u : 1u);
+            for (int kk = 0; kk < BN / 32; ++kk)
+              umma_ts(tO, tP + kk * 8, vd + ((kk * 2048) >> 4), IDESC_PV, (i == 0 && kk == 0) ? 0u : 1u);
+          }
+          __syncwarp();
           if (!mbar_poll(pbar + 8, pph, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
           tc_fence_after();
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = BN / 32; kk < BN / 16; ++kk) umma_ts(tO, tP + kk * 8, vd + ((kk * 2048) >> 4), IDESC_PV, 1u);
-          // O of this job is final after its last PV: the epilogue's signal.  (The
-          // softmax needs no per-PV signal: the S_q(i + 1) commit covers PV_q(i).)
-          if (i == tiles[q] - 1) umma_commit(BAR(o_full[0]) + 8 * q);
+            for (int kk = BN / 32; kk < BN / 16; ++kk) umma_ts(tO, tP + kk * 8, vd + ((kk * 2048) >> 4), IDESC_PV, 1u);
+            // O of this job is final after its last PV: the epilogue's signal.  (The
+            // softmax needs no per-PV signal: the S_q(i + 1) commit covers PV_q(i).)
+            if (i == tiles[q] - 1) umma_commit(BAR(o_full[0]) + 8 * q);
+            if (q == NQ - 1 || i >= tiles[NQ - 1]) umma_commit(BAR(v_empty[0]) + 8 * st);
+          }
+          __syncwarp();
           ++cnt_pv[q];
-          if (q == NQ - 1 || i >= tiles[NQ - 1]) umma_commit(BAR(v_empty[0]) + 8 * st);
           return true;
         };
         // prologue: S of key tile 0 for every active query tile; then per key
@@ -464,7 +476,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         n += P.n_tiles;
       }
       // drain: every issued tcgen05 op completes before TMEM is released
-      umma_commit(BAR(drain));
+      // (tcgen05 ops complete in issue order, and the elected lanes of one
+      // warp issue in program order)
+      __syncwarp();
+      if (elect_one()) umma_commit(BAR(drain));
+      __syncwarp();
       const long long t0 = clock64();
       while (!mbar_try_wait(BAR(drain), 0)) {
         if (clock64() - t0 > kWaitTimeoutCycles) {
