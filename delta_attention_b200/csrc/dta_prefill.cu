@@ -75,12 +75,10 @@ cudaError_t launch_anchor_delta(const float* dense, const float* sparse, __nv_bf
 
 }  // namespace dta
 
-#if DTA_PREFILL_NQ == 2
 namespace dta {
 
 constexpr int BM = 128;
 constexpr int BN = PREFILL_BN;  // keys per tile
-constexpr int S_BUFS = (BN == 64) ? 2 : 1;  // S buffers per query tile
 constexpr int NUM_THREADS = 128 + PREFILL_NQ * 128;
 constexpr int CTRL_BYTES = 2048;
 #ifndef DTA_REGS_CTRL
@@ -94,22 +92,7 @@ constexpr int REGS_LAUNCH = (65536 / NUM_THREADS) & ~7;
 constexpr int REGS_CTRL = DTA_REGS_CTRL, REGS_SOFTMAX = DTA_REGS_SOFTMAX;
 static_assert(128 * REGS_CTRL + PREFILL_NQ * 128 * REGS_SOFTMAX <= NUM_THREADS * REGS_LAUNCH,
               "register split exceeds the launch budget");
-// Q tile slots: with 2 (the default), tile q keeps slot q; with 3, tile A keeps slot 0 and
-// tile B rotates over the other two, so the next job's Q_B can load while this job still
-// runs.  Measured at config 2: 2 slots and a third K stage 7.63 ms per step, 3 slots and two
-// K stages 8.11 ms.
-#ifndef DTA_Q_SLOTS
-#define DTA_Q_SLOTS 2
-#endif
-constexpr int Q_SLOTS = DTA_Q_SLOTS;
-static_assert(Q_SLOTS == 2 || Q_SLOTS == 3, "Q slots");
 constexpr int NQ = PREFILL_NQ;
-// Element pairs (of the 16 per 32-column chunk) whose exponentials run on the
-// FMA pipe (exp2_poly) instead of the MUFU unit.
-#ifndef DTA_POLY_PAIRS
-#define DTA_POLY_PAIRS 0
-#endif
-constexpr int POLY_PAIRS = DTA_POLY_PAIRS;
 
 template <int HD>
 struct Geo {
@@ -124,26 +107,26 @@ struct Geo {
 #ifndef DTA_V_STAGES
 #define DTA_V_STAGES 2
 #endif
-  static constexpr int K_STAGES = (BN == 64) ? 4 : DTA_K_STAGES;
-  static constexpr int V_STAGES = (BN == 64) ? 4 : DTA_V_STAGES;
+  static constexpr int K_STAGES = DTA_K_STAGES;
+  static constexpr int V_STAGES = DTA_V_STAGES;
   static constexpr int Q_OFF = CTRL_BYTES;
-  static constexpr int K_OFF = Q_OFF + Q_SLOTS * TILE_BYTES;
+  static constexpr int K_OFF = Q_OFF + NQ * TILE_BYTES;  // one Q slot per query tile
   static constexpr int V_OFF = K_OFF + K_STAGES * KV_TILE_BYTES;
   // staging tile of the window launch's TMA-store epilogue (one 128-row bf16 tile)
   static constexpr int STG_OFF = V_OFF + V_STAGES * KV_TILE_BYTES;
   static constexpr int SMEM_BYTES = STG_OFF + TILE_BYTES + 1024;  // + alignment slack
   static constexpr int TMEM_COLS = 512;
-  static constexpr int S_COL = 0;    // S buffer b of tile q at (q * S_BUFS + b) * BN
+  static constexpr int S_COL = 0;    // S of tile q at q * BN
   static constexpr int O_COL = 256;  // O of tile q at 256 + q * 128
 };
 static_assert(Geo<128>::SMEM_BYTES <= 232448, "shared memory budget");
 
 struct Ctrl {
   uint64_t job_full[2], job_empty[2];
-  uint64_t q_full[Q_SLOTS], q_empty[Q_SLOTS];
+  uint64_t q_full[NQ], q_empty[NQ];
   uint64_t k_full[4], k_empty[4], v_full[4], v_empty[4];
-  // p_full[2 * (q * S_BUFS + b) + h]: half h of P (keys [h * BN/2, (h+1) * BN/2))
-  uint64_t s_full[NQ * S_BUFS], p_full[NQ * S_BUFS * 2], o_full[NQ], o_empty[NQ];
+  // p_full[2 * q + h]: half h of P_q (keys [h * BN/2, (h+1) * BN/2))
+  uint64_t s_full[NQ], p_full[NQ * 2], o_full[NQ], o_empty[NQ];
   uint64_t stg_full[NQ];    // tile q's rows are in the staging tile (4 warps)
   uint64_t stg_free;        // the staging tile's last TMA store has read it
   uint64_t drain;
@@ -186,7 +169,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       mbar_init(BAR(job_full[0]) + 8 * i, 1);
       mbar_init(BAR(job_empty[0]) + 8 * i, 1 + 4 * NQ);  // MMA thread + softmax warps
     }
-    for (int i = 0; i < Q_SLOTS; ++i) {
+    for (int i = 0; i < NQ; ++i) {
       mbar_init(BAR(q_full[0]) + 8 * i, 1);
       mbar_init(BAR(q_empty[0]) + 8 * i, 1);
     }
@@ -199,11 +182,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       mbar_init(BAR(v_empty[0]) + 8 * i, 1);
     }
     for (int q = 0; q < NQ; ++q) {
-      for (int b = 0; b < S_BUFS; ++b) {
-        mbar_init(BAR(s_full[0]) + 8 * (q * S_BUFS + b), 1);
-        mbar_init(BAR(p_full[0]) + 8 * (2 * (q * S_BUFS + b)), 4);
-        mbar_init(BAR(p_full[0]) + 8 * (2 * (q * S_BUFS + b) + 1), 4);
-      }
+      mbar_init(BAR(s_full[0]) + 8 * q, 1);
+      mbar_init(BAR(p_full[0]) + 8 * (2 * q), 4);
+      mbar_init(BAR(p_full[0]) + 8 * (2 * q + 1), 4);
       mbar_init(BAR(o_full[0]) + 8 * q, 1);
       mbar_init(BAR(o_empty[0]) + 8 * q, 4);  // softmax warps of tile q, after reading O
     }
@@ -499,7 +480,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int hh = r >> (__ffs(p.R) - 1);  // head of this row inside the KV group (R = 128 / G, a power of two)
     const int rr = r & (p.R - 1);
-    const uint32_t tS0 = tmem + lane_off + G::S_COL + q * S_BUFS * BN;
+    const uint32_t tS = tmem + lane_off + G::S_COL + q * BN;
     const uint32_t tO = tmem + lane_off + G::O_COL + q * 128;
     const float sl2 = p.scale_log2;
     int cnt = 0;        // S tiles consumed by this warpgroup (= PVs of its query tile)
@@ -550,9 +531,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       float m_run = -INFINITY, l_run = 0.f;
       bool aborted = false;
       for (int i = 0; i < T; ++i, ++cnt) {
-        const int sb = cnt % S_BUFS;  // S buffer of this tile
-        const uint32_t tS = tS0 + sb * BN;
-        if (!mbar_wait_warp(BAR(s_full[0]) + 8 * (q * S_BUFS + sb), (cnt / S_BUFS) & 1, abort_flag, err,
+        if (!mbar_wait_warp(BAR(s_full[0]) + 8 * q, cnt & 1, abort_flag, err,
                             KERR_TIMEOUT_SOFTMAX)) {
           aborted = true;
           break;
@@ -568,97 +547,113 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) tmem_ld32f(tS + c * 32, x + c * 32);
         tmem_wait_ld();
+        // column window of this row: valid iff A <= c <= Bq and not X <= c < Y,
+        // as one validity bit per column (32 per word), then one bit test and
+        // one select per element
+        const int mA = seg_lo - ks;
+        const int mB = min(seg_hi - 1, qpos) - ks;
+        const int mX = sink_q - ks;
+        const int mY = lo_q - ks;
+        auto mask_word = [&](int w) {
+          const int o = 32 * w;
+          const uint32_t m = bits_from(mA - o) & ~bits_from(mB + 1 - o) & ~(bits_from(mX - o) & ~bits_from(mY - o));
+#pragma unroll
+          for (int e = 0; e < 32; ++e) x[o + e] = ((m >> e) & 1u) ? x[o + e] : -INFINITY;
+        };
         if (!full) {
-          // column window of this row: valid iff A <= c <= Bq and not X <= c < Y
-          const int A = seg_lo - ks;
-          const int Bq = min(seg_hi - 1, qpos) - ks;
-          const int X = sink_q - ks;
-          const int Y = lo_q - ks;
-          // as one validity bit per column (32 per word), then one bit test and
-          // one select per element
 #pragma unroll
-          for (int w = 0; w < BN / 32; ++w) {
-            const int o = 32 * w;
-            const uint32_t m = bits_from(A - o) & ~bits_from(Bq + 1 - o) & ~(bits_from(X - o) & ~bits_from(Y - o));
+          for (int w = 0; w < BN / 32; ++w) mask_word(w);
+        }
+        // row max: 8 independent chains of three-input maxima (scaled, log2 domain)
+        auto row_max = [&]() -> float {
+          float mk[8];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) x[o + e] = ((m >> e) & 1u) ? x[o + e] : -INFINITY;
+          for (int k = 0; k < 8; ++k) {
+            float m = fmax3(x[k], x[k + 8], x[k + 16]);
+#pragma unroll
+            for (int j = 3; j + 1 < BN / 8; j += 2) m = fmax3(m, x[k + 8 * j], x[k + 8 * (j + 1)]);
+            mk[k] = fmaxf(m, x[k + BN - 8]);
           }
-        }
-        // row max: 8 independent chains of three-input maxima
-        float mk[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          float m = fmax3(x[k], x[k + 8], x[k + 16]);
-#pragma unroll
-          for (int j = 3; j + 1 < BN / 8; j += 2) m = fmax3(m, x[k + 8 * j], x[k + 8 * (j + 1)]);
-          mk[k] = fmaxf(m, x[k + BN - 8]);
-        }
-        float mt = fmax3(fmax3(mk[0], mk[1], mk[2]), fmax3(mk[3], mk[4], mk[5]), fmaxf(mk[6], mk[7]));
-        mt *= sl2;  // scaled units (log2 domain); -inf stays -inf
-        // keep the running max unless it grows by more than 2^8 (exact: O and
-        // l always share the reference max; P stays <= 256)
-        const bool need = (i > 0) && (mt > m_run + 8.0f);
-        const float m_new = (i == 0 || need) ? mt : m_run;
-        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        // P = exp2(S * scale - m): scale/shift and row sums on packed fp32
-        // pairs; POLY_PAIRS of every 16 pairs take the FMA-pipe exponential
+          return fmax3(fmax3(mk[0], mk[1], mk[2]), fmax3(mk[3], mk[4], mk[5]), fmaxf(mk[6], mk[7])) * sl2;
+        };
+        // The running max is kept unless a tile raises it by more than 2^8
+        // (exact: O and l always share the reference max; P stays <= 256).  So
+        // after the first tile of a job the exponentials of the first 32 keys
+        // start from the running max while this tile's max is computed beside
+        // them; in the rare case that it grew too much, they are recomputed.
+        if (i == 0) m_run = row_max();
+        // P = exp2(S * scale - m): scale/shift and row sums on packed fp32 pairs
         const uint64_t sc2 = f2_pack(sl2, sl2);
-        const uint64_t nm2 = f2_pack(-m_use, -m_use);
         uint64_t ls2[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) ls2[k] = f2_pack(0.f, 0.f);
-        auto exp_chunk = [&](int c, uint32_t (&pk)[16]) {
+        auto exp_chunk = [&](int c, uint32_t (&pk)[16], uint64_t nm2) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             float a0, a1, p0, p1;
             f2_unpack(f2_fma(f2_pack(x[c * 32 + 2 * e], x[c * 32 + 2 * e + 1]), sc2, nm2), a0, a1);
-            const bool poly = POLY_PAIRS > 0 && (e % 16) * POLY_PAIRS % 16 >= 16 - POLY_PAIRS;
-            if (poly) {
-              exp2_poly2(a0, a1, p0, p1);
-            } else {
-              p0 = fast_exp2(a0);
-              p1 = fast_exp2(a1);
-            }
+            p0 = fast_exp2(a0);
+            p1 = fast_exp2(a1);
             ls2[e & 3] = f2_add(ls2[e & 3], f2_pack(p0, p1));
             pk[e] = pack_bf16x2(p0, p1);
           }
         };
-        const uint32_t pbar = BAR(p_full[0]) + 8 * (2 * (q * S_BUFS + sb));
+        auto neg_m = [](float m) { const float u = (m == -INFINITY) ? 0.f : m; return f2_pack(-u, -u); };
+        uint32_t pk0[16];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ls2[k] = f2_pack(0.f, 0.f);
+        exp_chunk(0, pk0, neg_m(m_run));
+        const float mt = row_max();
+        const bool need = (i > 0) && (mt > m_run + 8.0f);
+        const bool any_need = __any_sync(0xffffffffu, need);
+        const float m_old = m_run;
+        if (any_need) {
+          // rare: the max grew by more than 2^8 for some row of the warp.  Those
+          // rows redo the first 32 keys with the new max (and rescale O below)
+          const float m_new = need ? mt : m_run;
+          // S is still in TMEM (P has not been written): reload the first 32 keys
+          tmem_ld32f(tS, x);
+          tmem_wait_ld();
+          if (!full) mask_word(0);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) ls2[k] = f2_pack(0.f, 0.f);
+          exp_chunk(0, pk0, neg_m(m_new));
+          m_run = m_new;
+        }
+        const uint32_t pbar = BAR(p_full[0]) + 8 * (2 * q);
         __syncwarp();  // converge before the warp-collective TMEM stores
+        tmem_st16(tS, pk0);
+        {
+          uint32_t pk1[16];
+          exp_chunk(1, pk1, neg_m(m_run));
+          tmem_st16(tS + 16, pk1);
+        }
+        if (any_need) {
+          // O rescale for rows whose max moved (here, with half of the S row
+          // dead, to keep registers low).  The S_q(i) commit covers every
+          // earlier MMA, so PV(i-1) is complete; the TMEM round trip is
+          // warp-collective and other rows scale by 1.
+          const float alpha = !need ? 1.f : ((m_old == -INFINITY) ? 0.f : fast_exp2(m_old - m_run));
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t pk[16];
-          exp_chunk(c, pk);
-          if (c == BN / 64) {
-            // Rescale O when the running max grew by more than 2^8 (here, where
-            // half of the S row is already dead, to keep registers low).  The
-            // S_q(i) commit covers every earlier MMA of the issuer, so PV(i-1)
-            // is complete.  The TMEM round trip is warp-collective: lanes that
-            // keep their max scale by 1.
-            if (i > 0 && __any_sync(0xffffffffu, need)) {
-              const float alpha = !need ? 1.f : ((m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new));
+          for (int c2 = 0; c2 < HD / 32; ++c2) {
+            uint32_t o[32];
+            tmem_ld32(tO + c2 * 32, o);
+            tmem_wait_ld();
 #pragma unroll
-              for (int c2 = 0; c2 < HD / 32; ++c2) {
-                float o[32];
-                tmem_ld32f(tO + c2 * 32, o);
-                tmem_wait_ld();
-                uint32_t u[32];
-#pragma unroll
-                for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(o[e] * alpha);
-                tmem_st32(tO + c2 * 32, u);
-              }
-              if (need) l_run *= alpha;
-            }
-            // the first half of P (keys [0, BN/2)) is in TMEM: release it
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(pbar);
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + c2 * 32, o);
           }
+          if (need) l_run *= alpha;
+        }
+        // the first half of P (keys [0, BN/2)) is in TMEM: release it
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pbar);
+#pragma unroll
+        for (int c = BN / 64; c < BN / 32; ++c) {
+          uint32_t pk[16];
+          exp_chunk(c, pk, neg_m(m_run));
           tmem_st16(tS + c * 16, pk);
         }
-        if (aborted) break;
-        m_run = m_new;
         {
           float l0, l1;
           f2_unpack(f2_add(f2_add(ls2[0], ls2[1]), f2_add(ls2[2], ls2[3])), l0, l1);
@@ -819,4 +814,3 @@ cudaError_t launch_prefill(const PrefillParams& p, int head_dim, int grid, cudaS
 }
 
 }  // namespace dta
-#endif  // DTA_PREFILL_NQ == 2

@@ -10,13 +10,9 @@ namespace dta {
 
 enum Launch : int { LAUNCH_ROWS = 0, LAUNCH_WINDOW = 1 };
 
-// Query tiles (of 128 rows = R rows x G heads) per kernel job: 2 selects the
-// ping-pong kernel (dta_prefill.cu), 1 the double-buffered kernel
-// (dta_prefill1.cu).
-#ifndef DTA_PREFILL_NQ
-#define DTA_PREFILL_NQ 2
-#endif
-constexpr int PREFILL_NQ = DTA_PREFILL_NQ;
+// Query tiles (of 128 rows = R rows x G heads) per kernel job: the two tiles
+// of a job ping-pong on the tensor core (dta_prefill.cu).
+constexpr int PREFILL_NQ = 2;
 // Keys per K/V tile (the TMA box height of the K and V tensor maps).
 constexpr int PREFILL_BN = 128;
 

@@ -45,12 +45,6 @@ __device__ __forceinline__ void mbar_init_fence() {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-// Arrive without release semantics: the arriving thread's earlier global
-// stores are not waited for.  Used where the consumer only depends on TMEM
-// accesses that tcgen05 fences already order.
-__device__ __forceinline__ void mbar_arrive_relaxed(uint32_t bar) {
-  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
@@ -125,23 +119,8 @@ static __device__ __forceinline__ bool mbar_poll_slow(uint32_t bar, uint32_t par
 }
 __device__ __forceinline__ bool mbar_poll(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
                                           int code) {
-#ifdef DTA_POLL_INLINE
-  const long long t0 = clock64();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_test(bar, parity)) return true;
-    if ((it & 1023u) == 0u) {
-      if (*abort_flag) return false;
-      if (clock64() - t0 > kWaitTimeoutCycles) {
-        *abort_flag = 1;
-        atomicCAS(err, 0, code);
-        return false;
-      }
-    }
-  }
-#else
   if (mbar_test(bar, parity)) return true;
   return mbar_poll_slow(bar, parity, abort_flag, err, code);
-#endif
 }
 
 // Warp-collective variant: every lane waits, then the warp reconverges so the
@@ -371,11 +350,6 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
-__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
 
 // 2^x evaluated on the FMA pipe instead of the MUFU unit.  Range reduction
 // x = n + f with n = rint(x) (the 1.5 * 2^23 shifter leaves rint(x) in the low
@@ -394,23 +368,6 @@ __device__ __forceinline__ float exp2_poly(float x) {
   p = __fmaf_rn(p, f, 0.6932609854606553f);
   p = __fmaf_rn(p, f, 0.9999280735394012f);
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-// exp2_poly on a pair, with the range reduction and the polynomial on packed
-// fp32x2 operations (half the FMA-pipe instructions of two scalar calls).
-__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
-  const uint64_t sh = f2_pack(12582912.0f, 12582912.0f);
-  const uint64_t x = f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
-  const uint64_t t = f2_add(x, sh);
-  const uint64_t f = f2_sub(x, f2_sub(t, sh));
-  uint64_t p = f2_fma(f2_pack(0.05517166905792616f, 0.05517166905792616f), f,
-                      f2_pack(0.2426111221932161f, 0.2426111221932161f));
-  p = f2_fma(p, f, f2_pack(0.6932609854606553f, 0.6932609854606553f));
-  p = f2_fma(p, f, f2_pack(0.9999280735394012f, 0.9999280735394012f));
-  float p0, p1, t0, t1;
-  f2_unpack(p, p0, p1);
-  f2_unpack(t, t0, t1);
-  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
 // 32-byte global store (one sector per lane)
