@@ -213,19 +213,25 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   cudaError_t e = cudaMemsetAsync(a->workspace, 0, kHeaderBytes, stream);
   if (e != cudaSuccess) return fail_cuda(e);
 
-  // launch 1: dense rows (anchors + tail) and sparse anchor rows
+  // With gamma = 64, uniform anchors and 4 heads per KV group, every 64-row job
+  // of the windowed launch starts at its anchor row, so that launch forms
+  // delta = dense - sparse itself from the anchor row's own sparse output and
+  // the rows launch skips the sparse anchor rows (and the delta kernel).  Both
+  // phases derive the choice from the arguments alone.
+  const bool fuse = a->mode == DTA_MODE_DELTA && !a->anchors && a->gamma == 64 && G == 4 && L.n_anchor > 0;
+  // launch 1: dense rows (anchors + tail) and, unless fused, sparse anchor rows
   if ((phases & DTA_PHASE_ROWS) && a->mode != DTA_MODE_SPARSE_ONLY && L.n_sel > 0) {
     dta::PrefillParams r = p;
     r.launch = dta::LAUNCH_ROWS;
     r.direct_from = (a->mode == DTA_MODE_DELTA) ? L.n_anchor : 0;
     r.n_dense_tiles = (L.n_sel + JR - 1) / JR;
-    r.n_sparse_tiles = (a->mode == DTA_MODE_DELTA) ? (L.n_anchor + JR - 1) / JR : 0;
+    r.n_sparse_tiles = (a->mode == DTA_MODE_DELTA && !fuse) ? (L.n_anchor + JR - 1) / JR : 0;
     r.n_jobs = (r.n_dense_tiles + r.n_sparse_tiles) * B * Hkv;
     const int grid = r.n_jobs < sms ? r.n_jobs : sms;
     if ((e = dta::launch_prefill(r, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
   }
   // delta = dense - sparse per anchor (bf16 for the windowed launch, fp32 telemetry on request)
-  if ((phases & DTA_PHASE_ROWS) && L.buf_bytes) {
+  if ((phases & DTA_PHASE_ROWS) && L.buf_bytes && !fuse) {
     const long long n = (long long)B * L.n_anchor * H * d;
     if ((e = dta::launch_anchor_delta(p.dense_buf, p.sparse_buf, delta_buf, a->anchor_delta, n, stream)) !=
         cudaSuccess)
@@ -235,6 +241,8 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   if (phases & DTA_PHASE_WINDOW) {
     dta::PrefillParams w = p;
     w.launch = dta::LAUNCH_WINDOW;
+    w.fuse_delta = fuse;
+    w.anchor_delta_f32 = fuse ? a->anchor_delta : nullptr;
     // out [B, S, H, d] seen as (d, s, H, B) with a (64, R, G, 1) box: one box is
     // one query tile, rows in the tile's order (head-major), so full tiles
     // leave the kernel with a TMA store; without a map the kernel stores rows

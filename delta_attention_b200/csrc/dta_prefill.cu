@@ -129,7 +129,10 @@ struct Ctrl {
   uint64_t s_full[NQ], p_full[NQ * 2], o_full[NQ], o_empty[NQ];
   uint64_t stg_full[NQ];    // tile q's rows are in the staging tile (4 warps)
   uint64_t stg_free;        // the staging tile's last TMA store has read it
+  uint64_t delta_ready;     // fused delta: tile A wrote this job's anchor rows (4 warps)
+  uint64_t delta_free;      // fused delta: tile B read them (4 warps)
   uint64_t drain;
+  uint32_t dslot[4][64];    // fused delta: bf16 (dense - sparse) row of each head's anchor
   int job[2][8];
   Plan plan[2];             // key-tile plan of job[slot], computed once by the producer
   uint32_t tmem_base;
@@ -190,6 +193,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     }
     for (int q = 0; q < NQ; ++q) mbar_init(BAR(stg_full[0]) + 8 * q, 4);
     mbar_init(BAR(stg_free), 1);
+    mbar_init(BAR(delta_ready), 4);
+    mbar_init(BAR(delta_free), 4);
     mbar_init(BAR(drain), 1);
     ctrl->abort_flag = 0;
     mbar_init_fence();
@@ -486,6 +491,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     int cnt = 0;        // S tiles consumed by this warpgroup (= PVs of its query tile)
     int jobs_done = 0;  // jobs in which this query tile was active
     int stg_uses = 0;   // uses of the staging tile by both warpgroups so far
+    int f_writes = 0;   // fused delta: anchor rows published by tile A so far
+    int f_reads = 0;    // fused delta: of those, read by tile B
     int my_stg = 0;     // uses by this warpgroup
     for (int it = 0;; ++it) {
       const int slot = it & 1;
@@ -511,6 +518,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       const bool use_stg = q ? stg_b : stg_a;
       const int stg_use = stg_uses + ((q == 1 && stg_a) ? 1 : 0);  // index of this tile's use
       stg_uses += (stg_a ? 1 : 0) + (stg_b ? 1 : 0);
+      // fused delta (windowed launch, gamma 64, 4 heads per group): tile A's
+      // row 0 of each head is the job's anchor; tile A publishes dense - sparse
+      // for it and tile B reads it.  Both warpgroups count every job.
+      const bool fuse = p.fuse_delta && J.kind == JOB_WINDOW;
+      const int f_writes_prev = f_writes, f_reads_prev = f_reads;
+      if (fuse && P.tiles_t[0] > 0) ++f_writes;
+      if (fuse && P.tiles_t[0] > 0 && P.tiles_t[1] > 0) ++f_reads;
       if (T == 0) continue;  // this query tile is empty in this job
       const int li = q * p.R + rr;  // job-local row
       const bool row_valid = li < J.count;
@@ -522,8 +536,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       // the owning anchor's delta row (window launch, delta mode), pulled into
       // L1 now for the epilogue at the end of the job
       const __nv_bfloat16* dlt = nullptr;
-      if (J.kind == JOB_WINDOW && p.mode == 0 && p.delta_buf) {
-        dlt = p.delta_buf + (((long long)J.b * p.n_anchor + anchor_of(p, qpos)) * p.H + J.g * p.G + hh) * HD;
+      const long long anchor_row = ((long long)J.b * p.n_anchor + anchor_of(p, qpos)) * p.H + J.g * p.G + hh;
+      float4 dn4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (fuse) {
+        // tile A: each lane holds 4 columns of its head's anchor dense row (fp32,
+        // written by the rows launch), loaded now, used at the end of the job
+        if (q == 0) dn4 = __ldg(reinterpret_cast<const float4*>(p.dense_buf + anchor_row * HD) + (lane & (HD / 4 - 1)));
+      } else if (J.kind == JOB_WINDOW && p.mode == 0 && p.delta_buf) {
+        dlt = p.delta_buf + anchor_row * HD;
         asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char*>(dlt) + (lane & (HD * 2 / 128 - 1)) * 128));
       }
       const int lo_max_t = q ? P.lo_max_t[1] : P.lo_max_t[0];
@@ -711,17 +731,52 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(o_empty[0]) + 8 * q);
       ++jobs_done;
-      if (use_stg) {
-        // the previous user's TMA store must have read the staging tile
-        if (stg_use > 0 && !mbar_wait_warp(BAR(stg_free), (stg_use - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX))
+      // the previous user's TMA store must have read the staging tile
+      if (use_stg && stg_use > 0 &&
+          !mbar_wait_warp(BAR(stg_free), (stg_use - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX))
+        break;
+      // the anchor's bf16 delta row: global (dlt) or, fused, this head's slot
+      const uint4* dsrc = reinterpret_cast<const uint4*>(dlt);
+      if (fuse) {
+        if (q == 0) {
+          // the slot is free once tile B has read the previous job's rows
+          if (f_reads_prev > 0 &&
+              !mbar_wait_warp(BAR(delta_free), (f_reads_prev - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX))
+            break;
+          // lane 0's row is the anchor (position J.start).  Its sparse row
+          // (O / l, exactly as the rows launch would store it) goes through the
+          // first 512 bytes of this warp's own staging rows, so that each lane
+          // forms dense - sparse for its 4 columns
+          float4* tmp = reinterpret_cast<float4*>(base + G::STG_OFF + quarter * 32 * 128);
+          if (lane == 0) {
+#pragma unroll
+            for (int c4 = 0; c4 < HD / 4; ++c4)
+              tmp[c4] = make_float4(o[4 * c4] * inv_l, o[4 * c4 + 1] * inv_l, o[4 * c4 + 2] * inv_l,
+                                    o[4 * c4 + 3] * inv_l);
+          }
+          __syncwarp();
+          if (lane < HD / 4) {
+            const float4 sp = tmp[lane];
+            const float4 d = make_float4(dn4.x - sp.x, dn4.y - sp.y, dn4.z - sp.z, dn4.w - sp.w);
+            ctrl->dslot[quarter][2 * lane] = pack_bf16x2(d.x, d.y);
+            ctrl->dslot[quarter][2 * lane + 1] = pack_bf16x2(d.z, d.w);
+            if (p.anchor_delta_f32) reinterpret_cast<float4*>(p.anchor_delta_f32 + anchor_row * HD)[lane] = d;
+          }
+          __syncwarp();  // the slot is complete and the staging rows may be overwritten
+          if (lane == 0) mbar_arrive(BAR(delta_ready));
+        } else if (!mbar_wait_warp(BAR(delta_ready), f_writes_prev & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
           break;
+        }
+        dsrc = reinterpret_cast<const uint4*>(&ctrl->dslot[quarter][0]);
+      }
+      if (use_stg) {
         // row r of the tile (head r / R, position r % R: the order of the
         // (64, R, G, 1) box) as 128-byte-swizzled 128-byte rows, one region per
         // 64 columns; o / l + delta on packed fp32 pairs
         const uint32_t stg = base_u32 + G::STG_OFF;
 #pragma unroll
         for (int c16 = 0; c16 < HD / 8; ++c16) {
-          const uint4 dv = dlt ? __ldg(reinterpret_cast<const uint4*>(dlt) + c16) : make_uint4(0, 0, 0, 0);
+          const uint4 dv = dsrc ? dsrc[c16] : make_uint4(0, 0, 0, 0);
           const uint32_t dw4[4] = {dv.x, dv.y, dv.z, dv.w};
           uint32_t w[4];
 #pragma unroll
@@ -761,7 +816,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           uint32_t ww[16];
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
-            const uint4 w = dlt ? __ldg(reinterpret_cast<const uint4*>(dlt) + c * 4 + v4) : make_uint4(0, 0, 0, 0);
+            const uint4 w = dsrc ? dsrc[c * 4 + v4] : make_uint4(0, 0, 0, 0);
             ww[4 * v4] = w.x; ww[4 * v4 + 1] = w.y; ww[4 * v4 + 2] = w.z; ww[4 * v4 + 3] = w.w;
           }
 #pragma unroll
@@ -783,6 +838,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         for (int e = 0; e < HD; e += 4)
           *reinterpret_cast<float4*>(dst_f + e) =
               make_float4(o[e] * inv_l, o[e + 1] * inv_l, o[e + 2] * inv_l, o[e + 3] * inv_l);
+      }
+      if (fuse && q == 1) {
+        __syncwarp();  // every lane has read the slot
+        if (lane == 0) mbar_arrive(BAR(delta_free));
       }
     }
   }

@@ -47,6 +47,12 @@ struct PrefillParams {
   float* dense_buf;             // [B, n_anchor, H, d] fp32
   float* sparse_buf;            // [B, n_anchor, H, d] fp32
   const __nv_bfloat16* delta_buf;  // [B, n_anchor, H, d] bf16: dense - sparse (window launch)
+  // window launch: form delta = dense - sparse inside the kernel from each job's
+  // own anchor row (gamma == 64 with 4 heads per KV group: a 64-row job starts at
+  // its anchor, which is row 0 of tile A for every head); the rows launch then
+  // computes no sparse anchor rows
+  int fuse_delta;
+  float* anchor_delta_f32;      // optional fp32 dense - sparse per anchor (telemetry)
   __nv_bfloat16* out;           // [B, out_rows, H, d]
   int tma_out;                  // window launch: full tiles leave through tm_out (TMA stores)
 };
