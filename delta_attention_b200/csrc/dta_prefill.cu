@@ -537,11 +537,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       // L1 now for the epilogue at the end of the job
       const __nv_bfloat16* dlt = nullptr;
       const long long anchor_row = ((long long)J.b * p.n_anchor + anchor_of(p, qpos)) * p.H + J.g * p.G + hh;
-      float4 dn4 = make_float4(0.f, 0.f, 0.f, 0.f);
       if (fuse) {
-        // tile A: each lane holds 4 columns of its head's anchor dense row (fp32,
-        // written by the rows launch), loaded now, used at the end of the job
-        if (q == 0) dn4 = __ldg(reinterpret_cast<const float4*>(p.dense_buf + anchor_row * HD) + (lane & (HD / 4 - 1)));
+        // tile A: its head's anchor dense row (fp32, written by the rows launch)
+        // goes to L2 now; each lane loads 4 columns of it at the end of the job
+        if (q == 0 && lane < HD * 4 / 128)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(p.dense_buf + anchor_row * HD) + lane * 128));
       } else if (J.kind == JOB_WINDOW && p.mode == 0 && p.delta_buf) {
         dlt = p.delta_buf + anchor_row * HD;
         asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char*>(dlt) + (lane & (HD * 2 / 128 - 1)) * 128));
@@ -719,6 +719,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
                          ? (mode_out == 1 ? p.dense_buf : p.sparse_buf) +
                                (((long long)J.b * p.n_anchor + gli) * p.H + h) * HD
                          : nullptr;
+      // (fused delta, tile A: this lane's 4 columns of the anchor's dense row,
+      // loaded while the last PV runs)
+      const float4 dn4 = (fuse && q == 0)
+                             ? __ldg(reinterpret_cast<const float4*>(p.dense_buf + anchor_row * HD) + (lane & (HD / 4 - 1)))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
       // o_full[q] completes once per job of this tile (after its last PV); the
       // next job's first PV waits for o_empty[q], so phases cannot run ahead
       if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, jobs_done & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;

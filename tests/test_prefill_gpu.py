@@ -96,6 +96,24 @@ def test_identities_gamma1_is_dense_and_full_window():
     assert rel < 1e-2, rel
 
 
+@pytest.mark.parametrize("batch,Hkv", [(1, 2), (2, 1)])
+def test_fused_anchor_delta_matches_oracle(batch, Hkv):
+    """gamma = 64 with 4 query heads per KV head: the windowed launch forms the
+    anchors' sparse rows and dense - sparse itself; the fp32 telemetry it writes
+    must match the oracle's dense minus sparse rows at every anchor."""
+    s, d, gamma, window, sink = 1024, 128, 64, 256, 64
+    H = 4 * Hkv
+    q, k, v = make_inputs(s, H, Hkv, d, seed=31 + batch, batch=batch)
+    out, delta = _run(q, k, v, gamma=gamma, window=window, sink=sink, return_anchor_delta=True)
+    torch.cuda.synchronize()
+    anchors, _, _ = orc.anchor_layout(s, gamma)
+    sc = d ** -0.5
+    qf, kf, vf = q.float(), k.float(), v.float()
+    ref = orc.dense_rows(qf, kf, vf, anchors, sc) - orc.sparse_rows(qf, kf, vf, anchors, window, sink, sc)
+    assert_close(delta.cpu(), ref, "fused anchor delta")
+    assert_close(out.cpu(), _oracle_full(q, k, v, gamma, window, sink), "fused delta output")
+
+
 def test_anchor_rows_equal_dense():
     """Reference T2: anchor and tail rows of the corrected output equal dense."""
     s, H, Hkv, d, gamma = 2048, 8, 2, 128, 64
