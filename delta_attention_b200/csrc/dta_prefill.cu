@@ -3,29 +3,34 @@
 //
 //   launch "rows"   : key-dense causal attention for an explicit list of query
 //                     rows (anchors + dense tail; the qsa_kernel contract of
-//                     delta_attention/delta_kernel.py:57-70) and key-sparse
-//                     attention for the anchor rows (needed to form the delta).
-//                     Jobs are ordered longest-first and fetched from an atomic
-//                     counter, so the triangular work of the anchor rows
-//                     balances over the SMs without split-K.
+//                     delta_attention/delta_kernel.py:57-70) and, unless the
+//                     window launch forms the delta itself (fuse_delta), key-
+//                     sparse attention for the anchor rows.  Jobs are ordered
+//                     longest-first and fetched from an atomic counter, so the
+//                     triangular work of the anchor rows balances over the SMs
+//                     without split-K.
 //   launch "window" : key-sparse attention (sink + block-anchored sliding
 //                     window, delta_attention/train/flex_delta.py:59-61) for
 //                     every row below s_p, with the delta correction of
 //                     delta_attention/llama.py:733-757 fused into the epilogue:
 //                     out = sparse + (dense[a] - sparse[a]) for the owning anchor
-//                     a.  The sparse output never goes to HBM.
+//                     a.  The sparse output never goes to HBM.  With fuse_delta
+//                     (gamma 64, 4 heads per KV group) each job's tile A holds
+//                     the job's anchor row and forms dense - sparse for it.
 //
 // A job is two 128-row query tiles ("A" and "B"); a tile is R rows x G heads of
 // one KV group (R = 128 / G), so the whole GQA group shares every K/V tile.
 // Three warpgroups (384 threads, launched at REGS_LAUNCH registers each and
 // re-split with setmaxnreg: control REGS_CTRL, softmax REGS_SOFTMAX):
-//   warp 0       : producer (job fetch, Q by TMA or cp.async gather into two Q
-//                  slots, K by TMA into a 3-stage ring, V into a 2-stage ring)
-//   warp 1       : TMEM owner; lane 0 issues every tcgen05.mma and commit
+//   warp 0       : producer (job fetch and key-tile plan, Q by TMA or cp.async
+//                  gather into two Q slots, K and V by TMA into 2-stage rings)
+//   warp 1       : TMEM owner and MMA issuer: the warp runs the issue loop and
+//                  one elected lane issues every tcgen05.mma and commit
 //   warps 2, 3   : idle
 //   warps 4..7   : softmax of tile A, one thread per row (TMEM lane); at the end
 //                  of a job the same warps read O, hand the accumulator back to
 //                  the MMA issuer and store the normalised, corrected rows
+//                  (full window tiles through a staging tile and a TMA store)
 //   warps 8..11  : softmax (and epilogue) of tile B
 // Each query tile has one S buffer in TMEM and the MMA issue order per key tile
 // i is PV_A(i), S_A(i+1), PV_B(i), S_B(i+1), so the softmax of one query tile
