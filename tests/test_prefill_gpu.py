@@ -96,12 +96,12 @@ def test_identities_gamma1_is_dense_and_full_window():
     assert rel < 1e-2, rel
 
 
-@pytest.mark.parametrize("batch,Hkv", [(1, 2), (2, 1)])
-def test_fused_anchor_delta_matches_oracle(batch, Hkv):
+@pytest.mark.parametrize("batch,Hkv,d", [(1, 2, 128), (2, 1, 128), (1, 2, 64)])
+def test_fused_anchor_delta_matches_oracle(batch, Hkv, d):
     """gamma = 64 with 4 query heads per KV head: the windowed launch forms the
     anchors' sparse rows and dense - sparse itself; the fp32 telemetry it writes
     must match the oracle's dense minus sparse rows at every anchor."""
-    s, d, gamma, window, sink = 1024, 128, 64, 256, 64
+    s, gamma, window, sink = 1024, 64, 256, 64
     H = 4 * Hkv
     q, k, v = make_inputs(s, H, Hkv, d, seed=31 + batch, batch=batch)
     out, delta = _run(q, k, v, gamma=gamma, window=window, sink=sink, return_anchor_delta=True)
