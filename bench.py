@@ -527,7 +527,9 @@ def run_b200(args, rank, world, local_rank):
             },
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": 2 * args.steps,
+            # two prefill launches per step, plus the delta kernel unless the
+            # windowed launch forms delta itself (gamma 64, 4 heads per KV head)
+            "gpu_launches": (2 if (args.gamma == 64 and G == 4) else 3) * args.steps,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
