@@ -119,7 +119,9 @@ struct Geo {
   static constexpr int V_OFF = K_OFF + K_STAGES * KV_TILE_BYTES;
   // staging tile of the window launch's TMA-store epilogue (one 128-row bf16 tile)
   static constexpr int STG_OFF = V_OFF + V_STAGES * KV_TILE_BYTES;
-  static constexpr int SMEM_BYTES = STG_OFF + TILE_BYTES + 1024;  // + alignment slack
+  // two staging halves of 128 rows x 128 bytes (64 bf16 columns), one per query tile
+  static constexpr int STG_HALF = 128 * 128;
+  static constexpr int SMEM_BYTES = STG_OFF + 2 * STG_HALF + 1024;  // + alignment slack
   static constexpr int TMEM_COLS = 512;
   static constexpr int S_COL = 0;    // S of tile q at q * BN
   static constexpr int O_COL = 256;  // O of tile q at 256 + q * 128
@@ -132,18 +134,19 @@ struct Ctrl {
   uint64_t k_full[4], k_empty[4], v_full[4], v_empty[4];
   // p_full[2 * q + h]: half h of P_q (keys [h * BN/2, (h+1) * BN/2))
   uint64_t s_full[NQ], p_full[NQ * 2], o_full[NQ], o_empty[NQ];
-  uint64_t stg_full[NQ];    // tile q's rows are in the staging tile (4 warps)
-  uint64_t stg_free;        // the staging tile's last TMA store has read it
+  uint64_t stg_full[NQ];    // tile q's rows are in its staging half (4 warps)
+  uint64_t stg_free[NQ];    // the last TMA store from tile q's staging half has read it
   uint64_t delta_ready;     // fused delta: tile A wrote this job's anchor rows (4 warps)
   uint64_t delta_free;      // fused delta: tile B read them (4 warps)
   uint64_t drain;
-  uint32_t dslot[4][64];    // fused delta: bf16 (dense - sparse) row of each head's anchor
+  alignas(16) uint32_t dslot[4][64];  // fused delta: bf16 (dense - sparse) row of each head's anchor (read as uint4)
   int job[2][8];
   Plan plan[2];             // key-tile plan of job[slot], computed once by the producer
   uint32_t tmem_base;
   int abort_flag;
 };
 static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block too large");
+static_assert(offsetof(Ctrl, dslot) % 16 == 0, "dslot is read with 16-byte loads");
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -196,8 +199,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       mbar_init(BAR(o_full[0]) + 8 * q, 1);
       mbar_init(BAR(o_empty[0]) + 8 * q, 4);  // softmax warps of tile q, after reading O
     }
-    for (int q = 0; q < NQ; ++q) mbar_init(BAR(stg_full[0]) + 8 * q, 4);
-    mbar_init(BAR(stg_free), 1);
+    for (int q = 0; q < NQ; ++q) {
+      mbar_init(BAR(stg_full[0]) + 8 * q, 4);
+      mbar_init(BAR(stg_free[0]) + 8 * q, 1);
+    }
     mbar_init(BAR(delta_ready), 4);
     mbar_init(BAR(delta_free), 4);
     mbar_init(BAR(drain), 1);
@@ -495,10 +500,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     const float sl2 = p.scale_log2;
     int cnt = 0;        // S tiles consumed by this warpgroup (= PVs of its query tile)
     int jobs_done = 0;  // jobs in which this query tile was active
-    int stg_uses = 0;   // uses of the staging tile by both warpgroups so far
+    int st_rounds = 0;  // 64-column TMA-store rounds through this tile's staging half
+    bool st_pending = false;  // (leader) the last round's store has not been waited for
     int f_writes = 0;   // fused delta: anchor rows published by tile A so far
     int f_reads = 0;    // fused delta: of those, read by tile B
-    int my_stg = 0;     // uses by this warpgroup
     for (int it = 0;; ++it) {
       const int slot = it & 1;
       if (!mbar_wait_warp(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
@@ -514,15 +519,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       // this warpgroup's tile: selects, not a dynamic index, so the plan stays in registers
       const int T = q ? P.tiles_t[1] : P.tiles_t[0];
       // Window-launch tiles whose 128 rows all lie below row_end leave through
-      // the staging tile and one TMA store (recompute mode skips anchor rows,
-      // so it stores row by row).  Both warpgroups count every use, A before B
-      // within a job, so each knows which release of the staging tile to wait for.
-      const bool stg_ok = p.tma_out && J.kind == JOB_WINDOW && p.mode != 1;
-      const bool stg_a = stg_ok && P.tiles_t[0] > 0 && J.start + p.R <= p.row_end;
-      const bool stg_b = stg_ok && P.tiles_t[1] > 0 && J.start + 2 * p.R <= p.row_end;
-      const bool use_stg = q ? stg_b : stg_a;
-      const int stg_use = stg_uses + ((q == 1 && stg_a) ? 1 : 0);  // index of this tile's use
-      stg_uses += (stg_a ? 1 : 0) + (stg_b ? 1 : 0);
+      // this tile's staging half and TMA stores (recompute mode skips anchor
+      // rows, so it stores row by row).
+      const bool use_stg = p.tma_out && J.kind == JOB_WINDOW && p.mode != 1 && T > 0 &&
+                           J.start + (q + 1) * p.R <= p.row_end;
       // fused delta (windowed launch, gamma 64, 4 heads per group): tile A's
       // row 0 of each head is the job's anchor; tile A publishes dense - sparse
       // for it and tile B reads it.  Both warpgroups count every job.
@@ -741,10 +741,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(o_empty[0]) + 8 * q);
       ++jobs_done;
-      // the previous user's TMA store must have read the staging tile
-      if (use_stg && stg_use > 0 &&
-          !mbar_wait_warp(BAR(stg_free), (stg_use - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX))
-        break;
+      // this tile's staging half is free once its last store has read it (the
+      // leader waits for that store only now, so it never holds up the warps)
+      const uint32_t half = base_u32 + G::STG_OFF + q * G::STG_HALF;
+      if (use_stg || fuse) {
+        if (quarter == 0 && lane == 0 && st_pending) {
+          bulk_wait_read_all();
+          mbar_arrive(BAR(stg_free[0]) + 8 * q);
+          st_pending = false;
+        }
+        if (st_rounds > 0 &&
+            !mbar_wait_warp(BAR(stg_free[0]) + 8 * q, (st_rounds - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX))
+          break;
+      }
       // the anchor's bf16 delta row: global (dlt) or, fused, this head's slot
       const uint4* dsrc = reinterpret_cast<const uint4*>(dlt);
       if (fuse) {
@@ -753,20 +762,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           if (f_reads_prev > 0 &&
               !mbar_wait_warp(BAR(delta_free), (f_reads_prev - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX))
             break;
-          // lane 0's row is the anchor (position J.start).  Its sparse row
-          // (O / l, exactly as the rows launch would store it) goes through the
-          // first 512 bytes of this warp's own staging rows, so that each lane
-          // forms dense - sparse for its 4 columns
-          float4* tmp = reinterpret_cast<float4*>(base + G::STG_OFF + quarter * 32 * 128);
+          // lane 0's row is the anchor (position J.start).  Its raw O row goes
+          // through the first 512 bytes of this warp's own staging rows; each
+          // lane scales its 4 columns by the anchor's 1/l (sparse = O / l, exactly
+          // as the rows launch would store it) and forms dense - sparse
+          float4* tmp = reinterpret_cast<float4*>(base + G::STG_OFF + quarter * 32 * 128);  // tile A's half
           if (lane == 0) {
 #pragma unroll
-            for (int c4 = 0; c4 < HD / 4; ++c4)
-              tmp[c4] = make_float4(o[4 * c4] * inv_l, o[4 * c4 + 1] * inv_l, o[4 * c4 + 2] * inv_l,
-                                    o[4 * c4 + 3] * inv_l);
+            for (int c4 = 0; c4 < HD / 4; ++c4) tmp[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
+            reinterpret_cast<float*>(tmp)[HD] = inv_l;
           }
           __syncwarp();
           if (lane < HD / 4) {
-            const float4 sp = tmp[lane];
+            const float inv_l0 = reinterpret_cast<const float*>(tmp)[HD];
+            const float4 ot = tmp[lane];
+            const float4 sp = make_float4(ot.x * inv_l0, ot.y * inv_l0, ot.z * inv_l0, ot.w * inv_l0);
             const float4 d = make_float4(dn4.x - sp.x, dn4.y - sp.y, dn4.z - sp.z, dn4.w - sp.w);
             ctrl->dslot[quarter][2 * lane] = pack_bf16x2(d.x, d.y);
             ctrl->dslot[quarter][2 * lane + 1] = pack_bf16x2(d.z, d.w);
@@ -781,43 +791,55 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       }
       if (use_stg) {
         // row r of the tile (head r / R, position r % R: the order of the
-        // (64, R, G, 1) box) as 128-byte-swizzled 128-byte rows, one region per
-        // 64 columns; o / l + delta on packed fp32 pairs
-        const uint32_t stg = base_u32 + G::STG_OFF;
-#pragma unroll
-        for (int c16 = 0; c16 < HD / 8; ++c16) {
-          const uint4 dv = dsrc ? dsrc[c16] : make_uint4(0, 0, 0, 0);
-          const uint32_t dw4[4] = {dv.x, dv.y, dv.z, dv.w};
-          uint32_t w[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int col = c16 * 8 + 2 * k;
-            const uint64_t d2 = f2_pack(__uint_as_float(dw4[k] << 16), __uint_as_float(dw4[k] & 0xffff0000u));
-            float a, b;
-            f2_unpack(f2_fma(f2_pack(o[col], o[col + 1]), inv2, d2), a, b);
-            w[k] = pack_bf16x2(a, b);
-          }
-          const int region = c16 >> 3, cw = c16 & 7;
-          st_shared_v4(stg + region * G::REGION_BYTES + r * 128 + ((cw ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(BAR(stg_full[0]) + 8 * q);
+        // (64, R, G, 1) box) as a 128-byte-swizzled 128-byte row of this tile's
+        // staging half, 64 columns per round; o / l + delta on packed fp32 pairs
         bool ok = true;
-        if (quarter == 0 && lane == 0) {
-          // leader: once all four warps wrote their rows, store the tile and
-          // release the staging tile when the store has read it
-          ok = mbar_wait(BAR(stg_full[0]) + 8 * q, my_stg & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX);
-          if (ok) {
-            for (int rg = 0; rg < G::REGIONS; ++rg)
-              tma_store_4d(&p.tm_out, stg + rg * G::REGION_BYTES, rg * 64, J.start + q * p.R, J.g * p.G, J.b);
-            bulk_commit_group();
-            bulk_wait_read_all();
-            mbar_arrive(BAR(stg_free));
+#pragma unroll
+        for (int rg = 0; rg < G::REGIONS; ++rg) {
+          if (rg > 0 &&
+              !mbar_wait_warp(BAR(stg_free[0]) + 8 * q, (st_rounds - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
+            ok = false;
+            break;
           }
+#pragma unroll
+          for (int cw = 0; cw < 8; ++cw) {
+            const int c16 = rg * 8 + cw;
+            const uint4 dv = dsrc ? dsrc[c16] : make_uint4(0, 0, 0, 0);
+            const uint32_t dw4[4] = {dv.x, dv.y, dv.z, dv.w};
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int col = c16 * 8 + 2 * k;
+              const uint64_t d2 = f2_pack(__uint_as_float(dw4[k] << 16), __uint_as_float(dw4[k] & 0xffff0000u));
+              float a, b;
+              f2_unpack(f2_fma(f2_pack(o[col], o[col + 1]), inv2, d2), a, b);
+              w[k] = pack_bf16x2(a, b);
+            }
+            st_shared_v4(half + r * 128 + ((cw ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(BAR(stg_full[0]) + 8 * q);
+          if (quarter == 0 && lane == 0) {
+            // leader: once all four warps wrote their rows, store the round; the
+            // half is released when the store has read it (for the tile's last
+            // round, at this tile's next use)
+            ok = mbar_wait(BAR(stg_full[0]) + 8 * q, st_rounds & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX);
+            if (ok) {
+              tma_store_4d(&p.tm_out, half, rg * 64, J.start + q * p.R, J.g * p.G, J.b);
+              bulk_commit_group();
+              if (rg + 1 < G::REGIONS) {
+                bulk_wait_read_all();
+                mbar_arrive(BAR(stg_free[0]) + 8 * q);
+              } else {
+                st_pending = true;
+              }
+            }
+          }
+          if (!__all_sync(0xffffffffu, ok)) break;
+          ++st_rounds;
         }
-        if (!__all_sync(0xffffffffu, ok)) break;
-        ++my_stg;
+        if (!ok) break;
       } else if (dst_bf) {
         // o / l + delta on packed fp32 pairs (one fma.rn.f32x2 per pair); the
         // delta row is shared by the warp's rows in the common case (L1 hits)
