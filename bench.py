@@ -554,10 +554,10 @@ def main():
     if world > 1:
         import datetime
 
-        # NCCL's version banner goes to stdout at NCCL_DEBUG=VERSION; rank 0's
-        # stdout must hold only the result line
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
+        # NCCL writes its log (version banner, communicator lines) to stdout;
+        # rank 0's stdout must hold only the result line, so the log goes to
+        # stderr at whatever NCCL_DEBUG level the caller chose
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)

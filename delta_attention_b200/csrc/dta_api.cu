@@ -8,22 +8,60 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "delta_attention_b200.h"
 #include "dta_decode.h"
+#include "dta_internal.h"
 #include "dta_prefill.h"
 
 namespace {
-
 thread_local int g_last_cuda_error = 0;
+}  // namespace
+
+namespace dta {
+
+int fail_cuda(cudaError_t e) {
+  g_last_cuda_error = (int)e;
+  (void)cudaGetLastError();  // clear the runtime's pending (non-sticky) error
+  return DTA_ERR_CUDA;
+}
+
+int check_device(int* sms) {
+  struct DeviceInfo {
+    int ok = -1;
+    int sms = 0;
+  };
+  static DeviceInfo info[64];
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e);
+  if (dev < 0 || dev >= 64) return DTA_ERR_UNSUPPORTED_DEVICE;
+  std::lock_guard<std::mutex> lock(mu);
+  if (info[dev].ok < 0) {
+    int major = 0, n = 0;
+    if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+      return fail_cuda(e);
+    if ((e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return fail_cuda(e);
+    info[dev].ok = (major == 10) ? 1 : 0;
+    info[dev].sms = n;
+  }
+  if (!info[dev].ok) return DTA_ERR_UNSUPPORTED_DEVICE;
+  *sms = info[dev].sms;
+  return DTA_OK;
+}
+
+}  // namespace dta
+
+namespace {
 
 constexpr size_t kHeaderBytes = 256;  // job counter, error word
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-inline int fail_cuda(cudaError_t e) {
-  g_last_cuda_error = (int)e;
-  return DTA_ERR_CUDA;
-}
+using dta::check_device;
+using dta::fail_cuda;
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -54,30 +92,6 @@ int encode_4d(CUtensorMap* map, const void* base, int d, long long rows, int hea
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? DTA_OK : DTA_ERR_CUDA;
-}
-
-struct DeviceInfo {
-  int ok = -1;
-  int sms = 0;
-};
-
-int check_device(int* sms) {
-  static DeviceInfo info[64];
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail_cuda(e);
-  if (dev < 0 || dev >= 64) return DTA_ERR_UNSUPPORTED_DEVICE;
-  if (info[dev].ok < 0) {
-    int major = 0, n = 0;
-    if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
-      return fail_cuda(e);
-    if ((e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return fail_cuda(e);
-    info[dev].ok = (major == 10) ? 1 : 0;
-    info[dev].sms = n;
-  }
-  if (!info[dev].ok) return DTA_ERR_UNSUPPORTED_DEVICE;
-  *sms = info[dev].sms;
-  return DTA_OK;
 }
 
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
@@ -150,6 +164,7 @@ const char* dta_status_string(int st) {
     case DTA_ERR_CUDA: return "CUDA runtime error";
     case DTA_ERR_UNSUPPORTED_DEVICE: return "device is not sm_100 (B200)";
     case DTA_ERR_KERNEL_TIMEOUT: return "kernel gave up on a bounded wait";
+    case DTA_ERR_SCRATCH_LIMIT: return "request needs more scratch than the no-alloc entry point's static array";
     default: return "unknown status";
   }
 }
@@ -352,6 +367,8 @@ static int decode_setup(const dta_decode_args* a, dta::DecodeParams* p, int sms)
   if (a->batch <= 0 || a->n_heads <= 0 || a->n_kv_heads <= 0 || a->n_keys <= 0) return DTA_ERR_SHAPE;
   if (a->head_dim != 64 && a->head_dim != 128) return DTA_ERR_HEAD_DIM;
   if (a->n_heads % a->n_kv_heads != 0 || a->n_heads / a->n_kv_heads > 8) return DTA_ERR_SHAPE;
+  // the kernels' grid y is batch x KV head (at most 65535)
+  if ((long long)a->batch * a->n_kv_heads > 65535) return DTA_ERR_SHAPE;
   if (a->window < 0 || a->sink < 0) return DTA_ERR_INVALID_ARG;
   memset(p, 0, sizeof(*p));
   const int n = a->n_keys;

@@ -7,6 +7,7 @@
 #include <mutex>
 
 #include "delta_attention_b200.h"
+#include "dta_internal.h"
 
 namespace {
 
@@ -21,13 +22,19 @@ std::mutex g_scratch_mu;
 // array's name is only a host-side stand-in, so the address is looked up with
 // cudaGetSymbolAddress once per device (that device current) and cached.
 int scratch_for_current_device(void** out) {
+  // an unsupported device is reported as such, before any symbol lookup
+  int sms = 0;
+  const int st = dta::check_device(&sms);
+  if (st != DTA_OK) return st;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return DTA_ERR_CUDA;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return dta::fail_cuda(e);
   if (dev < 0 || dev >= kMaxDevices) return DTA_ERR_UNSUPPORTED_DEVICE;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
   if (!g_scratch_addr[dev]) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || p == nullptr) return DTA_ERR_CUDA;
+    if ((e = cudaGetSymbolAddress(&p, g_decode_scratch)) != cudaSuccess) return dta::fail_cuda(e);
+    if (p == nullptr) return dta::fail_cuda(cudaErrorInvalidSymbol);
     g_scratch_addr[dev] = p;
   }
   *out = g_scratch_addr[dev];

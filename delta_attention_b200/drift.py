@@ -4,12 +4,12 @@
 (``ops.prefill(..., return_anchor_delta=True)``) instead of materialising
 them with torch ops; the summary format and histogram constants are the
 reference's (``delta_attention/drift.py:17-49``) so sidecar files aggregate
-with the reference's ``aggregate_drift``.
+with the reference's own tooling.
 """
 
 from __future__ import annotations
 
-from typing import Any, Dict, Iterable
+from typing import Any, Dict
 
 HIST_BINS = 40
 HIST_RANGE = (-1.0, 1.0)
@@ -32,22 +32,3 @@ def drift_summary(dense_sparse_diff, layer_idx: int, gamma: int, seq_len: int) -
         "p90": float(q[2].item()), "hist_bins": HIST_BINS, "hist_range": list(HIST_RANGE),
         "hist": [int(x) for x in hist.tolist()],
     }
-
-
-def aggregate_drift(lines: Iterable[Dict[str, Any]]) -> Dict[int, Dict[str, Any]]:
-    """n-weighted mean and summed histograms per layer (``delta_attention/drift.py:52-77``)."""
-    out: Dict[int, Dict[str, Any]] = {}
-    for s in lines:
-        layer = int(s["layer"])
-        if s["hist_bins"] != HIST_BINS or list(s["hist_range"]) != list(HIST_RANGE):
-            raise ValueError("drift sidecar bins/range do not match (mixed-version sidecar files)")
-        agg = out.setdefault(layer, {"layer": layer, "n": 0, "mean": 0.0, "requests": 0,
-                                     "hist": [0] * HIST_BINS, "hist_bins": HIST_BINS,
-                                     "hist_range": list(HIST_RANGE), "gamma": s["gamma"]})
-        total = agg["n"] + s["n"]
-        if total > 0:
-            agg["mean"] = (agg["mean"] * agg["n"] + s["mean"] * s["n"]) / total
-        agg["n"] = total
-        agg["requests"] += 1
-        agg["hist"] = [x + y for x, y in zip(agg["hist"], s["hist"])]
-    return out

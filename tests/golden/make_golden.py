@@ -231,9 +231,12 @@ def gen_decode(ref: str, out_dir: str) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("DTA_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("DTA_REFERENCE"),
+                    help="path of the reference checkout (or set DTA_REFERENCE)")
     ap.add_argument("--only", nargs="*")
     args = ap.parse_args()
+    if not args.reference:
+        raise SystemExit("pass --reference <checkout> or set DTA_REFERENCE")
     if not os.path.isdir(args.reference):
         raise SystemExit(f"reference checkout not found at {args.reference}")
     gen_stride(args.reference, HERE)
