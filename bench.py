@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--sink", type=int, default=128)
     ap.add_argument("--gamma", type=int, default=64)
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--split-tiles", type=int, default=0,
+                    help="key tiles per split-K chunk of the dense rows (0 = automatic)")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -372,9 +374,11 @@ def run_b200(args, rank, world, local_rank):
     k = apply_rope(k, cos, sin).bfloat16()
     del cos, sin
     out = torch.empty(U, N, G, d, dtype=torch.bfloat16, device=dev)
-    kw = dict(gamma=args.gamma, window=args.window, sink=args.sink, scaling=d ** -0.5)
+    kw = dict(gamma=args.gamma, window=args.window, sink=args.sink, scaling=d ** -0.5,
+              split_tiles=args.split_tiles)
     # one workspace, reused across steps (the kernels never allocate)
-    ws = ops.prefill_workspace(U, G, 1, N, d, gamma=args.gamma, device=dev)
+    ws = ops.prefill_workspace(U, G, 1, N, d, gamma=args.gamma, window=args.window, sink=args.sink,
+                               split_tiles=args.split_tiles, device=dev)
 
     def step(evs=None):
         if evs is not None:

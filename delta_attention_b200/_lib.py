@@ -14,7 +14,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("DTA_LIBRARY") or os.path.join(_HERE, "_lib", "libdelta_attention_b200.so")
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 DTA_OK = 0
 STATUS_NAMES = {
@@ -31,6 +31,18 @@ STATUS_NAMES = {
     10: "DTA_ERR_KERNEL_TIMEOUT",
     11: "DTA_ERR_SCRATCH_LIMIT",
 }
+
+# kernel codes written to the error word (dta_ptx.cuh)
+KERNEL_CODES = {
+    101: "producer wait ran out",
+    102: "MMA issuer wait ran out",
+    103: "softmax/epilogue wait ran out",
+    104: "tensor-core drain wait ran out",
+    105: "a query row or key limit outside the tensors (clamped; output not valid)",
+}
+
+# dta_prefill_args.flags / dta_rows_args.flags
+FLAG_TEST_STALL = 1
 
 MODES = {"delta": 0, "recompute": 1, "sparse-only": 2}
 
@@ -68,6 +80,7 @@ class PrefillArgs(ctypes.Structure):
         ("anchor_delta", c_vp),
         ("phases", c_i32),
         ("workspace", c_vp), ("workspace_bytes", ctypes.c_size_t),
+        ("error_word", c_vp), ("wait_cycles", c_i64), ("flags", c_i32), ("split_tiles", c_i32),
     ]
 
 
@@ -88,6 +101,7 @@ class RowsArgs(ctypes.Structure):
         ("out", c_vp),
         ("scaling", ctypes.c_float),
         ("workspace", c_vp), ("workspace_bytes", ctypes.c_size_t),
+        ("error_word", c_vp), ("wait_cycles", c_i64), ("flags", c_i32), ("split_tiles", c_i32),
     ]
 
 

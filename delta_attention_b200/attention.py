@@ -106,7 +106,8 @@ class DeltaAttention(torch.nn.Module):
                                   want_dense=True, want_sparse=False)
             return dense, None
         rows = torch.arange(s, device=query_states.device, dtype=torch.int32)
-        out = ops.rows(query_states, key_states, value_states, rows, rows + (n - s), scaling=scaling)
+        out = ops.rows(query_states, key_states, value_states, rows, rows + (n - s), scaling=scaling,
+                       validate=False)
         return out, None
 
     def _decode_sparse_row(self, q, k, v, scaling):
@@ -190,6 +191,12 @@ class DeltaAttention(torch.nn.Module):
         st["last_sparse"] = sparse_out
         self._dec_state = st
         return out, None
+
+    def check(self) -> None:
+        """Raise ``DtaError`` if a kernel launched on this layer's device since
+        the last check gave up on a bounded wait or met an out-of-range row
+        (synchronises the current stream; see ``ops.check_errors``)."""
+        ops.check_errors()
 
     def reset_decode_state(self) -> None:
         """Called at every new prefill (``delta_attention/sample.py:148-151``)."""

@@ -98,16 +98,79 @@ inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 inline bool stride_ok(long long s) { return s > 0 && (s * 2) % 16 == 0; }
 
 // ---------------------------------------------------------------------------
+// split-K plan of the rows launch's dense jobs
+// ---------------------------------------------------------------------------
+// The dense row tiles are cut into chunks of at most (total key tiles) /
+// (SMs * kSplitFactor) key tiles, so the longest row tile (the dense tail,
+// every key) no longer bounds the launch and the longest-first schedule
+// balances; chunks are never shorter than kSplitMinTiles (unless the caller
+// forces a chunk length).
+#ifndef DTA_SPLIT_FACTOR
+#define DTA_SPLIT_FACTOR 3
+#endif
+#ifndef DTA_SPLIT_MIN_TILES
+#define DTA_SPLIT_MIN_TILES 16
+#endif
+constexpr int kSplitFactor = DTA_SPLIT_FACTOR;
+constexpr int kSplitMinTiles = DTA_SPLIT_MIN_TILES;
+
+struct RowsSplit {
+  int n_dense_tiles = 0;
+  int c = 0, cmax = 1;     // PrefillParams::split_c / split_cmax
+  size_t cnt_bytes = 0;    // part_cnt, zeroed with the header
+  size_t part_o_bytes = 0, part_lse_bytes = 0;
+};
+
+// `tiles_of(t)` = key tiles of row tile t's longest row (estimated when the
+// rows come from a device list); `extra` = key tiles of the other jobs;
+// `forced` > 0 fixes the chunk length.
+template <class F>
+RowsSplit plan_rows_split(int BG, int n_sel, int JR, int head_dim, int sms, long long extra, int forced, F tiles_of) {
+  RowsSplit S;
+  S.n_dense_tiles = (n_sel + JR - 1) / JR;
+  long long total = extra;
+  int t_max = 1;
+  for (int t = 0; t < S.n_dense_tiles; ++t) {
+    const int T = tiles_of(t);
+    total += (long long)T * BG;
+    if (T > t_max) t_max = T;
+  }
+  const long long c0 = (total + (long long)sms * kSplitFactor - 1) / ((long long)sms * kSplitFactor);
+  const int chunk = forced > 0 ? forced : (int)(c0 < kSplitMinTiles ? kSplitMinTiles : c0);
+  const int cmax = (t_max + chunk - 1) / chunk;
+  if (cmax <= 1) return S;
+  S.cmax = cmax;
+  S.c = (t_max + cmax - 1) / cmax;
+  const size_t slots = (size_t)BG * S.n_dense_tiles * cmax * dta::PREFILL_NQ * 128;
+  S.part_o_bytes = align_up(slots * head_dim * 4, 256);
+  S.part_lse_bytes = align_up(slots * 4, 256);
+  S.cnt_bytes = align_up((size_t)BG * S.n_dense_tiles * dta::PREFILL_NQ * 4 * 4, 256);  // per warp
+  return S;
+}
+
+// SM count of the current device for sizing (148, a B200's, when there is none)
+int sizing_sms() {
+  int sms = 0;
+  if (check_device(&sms) != DTA_OK || sms <= 0) sms = 148;
+  return sms;
+}
+
+// ---------------------------------------------------------------------------
 // prefill layout
 // ---------------------------------------------------------------------------
+// workspace: header (job counter, error word) | split counters | dense_buf |
+// sparse_buf | delta_buf | split partials (O, lse)
 struct PrefillLayout {
   int s_p, n_anchor, n_sel;
+  bool fuse;           // the windowed launch forms delta itself (no sparse anchor jobs)
+  int n_sparse_tiles;  // sparse anchor row tiles of the rows launch
+  RowsSplit split;
   size_t buf_bytes;    // one of dense_buf / sparse_buf (fp32)
   size_t delta_bytes;  // delta_buf (bf16)
   size_t ws_bytes;
 };
 
-int prefill_layout(const dta_prefill_args* a, PrefillLayout* L) {
+int prefill_layout(const dta_prefill_args* a, int sms, PrefillLayout* L) {
   if (!a) return DTA_ERR_INVALID_ARG;
   if (a->abi_version != DTA_ABI_VERSION) return DTA_ERR_INVALID_ARG;
   if (a->batch <= 0 || a->n_heads <= 0 || a->n_kv_heads <= 0 || a->seq_len <= 0) return DTA_ERR_SHAPE;
@@ -116,14 +179,14 @@ int prefill_layout(const dta_prefill_args* a, PrefillLayout* L) {
   const int G = a->n_heads / a->n_kv_heads;
   if (G > 128 || 128 % G != 0) return DTA_ERR_SHAPE;
   if (a->mode < 0 || a->mode > 2) return DTA_ERR_INVALID_ARG;
-  if (a->window < 0 || a->sink < 0 || a->q_block <= 0) return DTA_ERR_INVALID_ARG;
+  if (a->window < 0 || a->sink < 0 || a->q_block <= 0 || a->split_tiles < 0) return DTA_ERR_INVALID_ARG;
   const int s = a->seq_len;
   if (a->mode == DTA_MODE_SPARSE_ONLY) {
     L->s_p = s;
     L->n_anchor = 0;
     L->n_sel = 0;
   } else if (a->anchors) {
-    if (a->n_anchors <= 0 || a->s_p <= 0 || a->s_p > s) return DTA_ERR_INVALID_ARG;
+    if (a->n_anchors <= 0 || a->s_p <= 0 || a->s_p > s || a->n_anchors > a->s_p) return DTA_ERR_INVALID_ARG;
     L->s_p = a->s_p;
     L->n_anchor = a->n_anchors;
     L->n_sel = a->n_anchors + (s - a->s_p);
@@ -136,10 +199,37 @@ int prefill_layout(const dta_prefill_args* a, PrefillLayout* L) {
     L->n_anchor = s_p / a->gamma;
     L->n_sel = L->n_anchor + cut_n;
   }
+  // With gamma = 64, uniform anchors and 4 heads per KV group, every 64-row job
+  // of the windowed launch starts at its anchor row, so that launch forms
+  // delta = dense - sparse itself from the anchor row's own sparse output and
+  // the rows launch skips the sparse anchor rows (and the delta kernel).  Both
+  // phases derive the choice from the arguments alone.
+  L->fuse = a->mode == DTA_MODE_DELTA && !a->anchors && a->gamma == 64 && G == 4 && L->n_anchor > 0;
+  const int R = 128 / G, JR = dta::PREFILL_NQ * R, BG = a->batch * a->n_kv_heads;
+  L->n_sparse_tiles = (a->mode == DTA_MODE_DELTA && !L->fuse) ? (L->n_anchor + JR - 1) / JR : 0;
+  if (L->n_sel > 0) {
+    // a sparse anchor tile spans its rows' window plus the rows' own spread
+    const long long sparse_tiles =
+        (long long)L->n_sparse_tiles * BG * ((a->window + a->sink) / dta::PREFILL_BN + 2);
+    const int n_anchor = L->n_anchor, s_p = L->s_p, n_sel = L->n_sel, gamma = a->gamma;
+    const bool uniform = !a->anchors;
+    auto tiles_of = [&](int t) {
+      const int i = (t + 1) * JR < n_sel ? (t + 1) * JR - 1 : n_sel - 1;  // last list row of tile t
+      long long pos;
+      if (i >= n_anchor) pos = s_p + (i - n_anchor);
+      else if (uniform) pos = (long long)i * gamma;
+      else pos = (long long)s_p * i / n_anchor;  // explicit anchors: spread estimate
+      return (int)(pos / dta::PREFILL_BN) + 1;
+    };
+    L->split = plan_rows_split(BG, L->n_sel, JR, a->head_dim, sms, sparse_tiles, a->split_tiles, tiles_of);
+  } else {
+    L->split = RowsSplit();
+  }
   const bool need_bufs = a->mode == DTA_MODE_DELTA && L->n_anchor > 0;
   L->buf_bytes = need_bufs ? align_up((size_t)a->batch * L->n_anchor * a->n_heads * a->head_dim * 4, 256) : 0;
   L->delta_bytes = need_bufs ? align_up((size_t)a->batch * L->n_anchor * a->n_heads * a->head_dim * 2, 256) : 0;
-  L->ws_bytes = kHeaderBytes + 2 * L->buf_bytes + L->delta_bytes;
+  L->ws_bytes = kHeaderBytes + L->split.cnt_bytes + 2 * L->buf_bytes + L->delta_bytes + L->split.part_o_bytes +
+                L->split.part_lse_bytes;
   return DTA_OK;
 }
 
@@ -171,26 +261,30 @@ const char* dta_status_string(int st) {
 
 size_t dta_prefill_workspace_size(const dta_prefill_args* a) {
   PrefillLayout L;
-  if (prefill_layout(a, &L) != DTA_OK) return 0;
+  if (prefill_layout(a, sizing_sms(), &L) != DTA_OK) return 0;
   return L.ws_bytes;
 }
 
 int dta_prefill(const dta_prefill_args* a, void* stream_) {
   PrefillLayout L;
-  int st = prefill_layout(a, &L);
+  int st = prefill_layout(a, 148, &L);  // argument checks (sized again below for this device)
   if (st != DTA_OK) return st;
+  if (!a->workspace) return DTA_ERR_WORKSPACE;
   if (!a->q || !a->k || !a->v || !a->out) return DTA_ERR_INVALID_ARG;
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out)) return DTA_ERR_ALIGNMENT;
   if (!stride_ok(a->q_stride_s) || !stride_ok(a->q_stride_h) || !stride_ok(a->q_stride_b) ||
       !stride_ok(a->k_stride_s) || !stride_ok(a->k_stride_h) || !stride_ok(a->k_stride_b) ||
       !stride_ok(a->v_stride_s) || !stride_ok(a->v_stride_h) || !stride_ok(a->v_stride_b))
     return DTA_ERR_STRIDE;
-  if (!a->workspace || a->workspace_bytes < L.ws_bytes || !aligned16(a->workspace)) return DTA_ERR_WORKSPACE;
   if (a->anchor_delta && (a->mode != DTA_MODE_DELTA || !aligned16(a->anchor_delta))) return DTA_ERR_INVALID_ARG;
   if (a->phases < 0 || a->phases > (DTA_PHASE_ROWS | DTA_PHASE_WINDOW)) return DTA_ERR_INVALID_ARG;
+  if (a->wait_cycles < 0 || (a->flags & ~DTA_FLAG_TEST_STALL) != 0) return DTA_ERR_INVALID_ARG;
+  if (a->error_word && ((uintptr_t)a->error_word & 3u) != 0) return DTA_ERR_ALIGNMENT;
   const int phases = a->phases ? a->phases : (DTA_PHASE_ROWS | DTA_PHASE_WINDOW);
   int sms = 0;
   if ((st = check_device(&sms)) != DTA_OK) return st;
+  if ((st = prefill_layout(a, sms, &L)) != DTA_OK) return st;
+  if (a->workspace_bytes < L.ws_bytes || !aligned16(a->workspace)) return DTA_ERR_WORKSPACE;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
 
   dta::PrefillParams p;
@@ -208,15 +302,26 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   p.anchors = a->anchors;
   p.mode = a->mode;
   p.out_rows = S;
+  p.seq_q = S;
+  p.kv_len = S;
   p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
+  p.wait_cycles = a->wait_cycles;
+  p.test_stall = (a->flags & DTA_FLAG_TEST_STALL) ? 1 : 0;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
   p.counter = reinterpret_cast<int*>(ws);
-  p.error = reinterpret_cast<int*>(ws) + 1;
-  p.dense_buf = L.buf_bytes ? reinterpret_cast<float*>(ws + kHeaderBytes) : nullptr;
-  p.sparse_buf = L.buf_bytes ? reinterpret_cast<float*>(ws + kHeaderBytes + L.buf_bytes) : nullptr;
-  __nv_bfloat16* delta_buf =
-      L.delta_bytes ? reinterpret_cast<__nv_bfloat16*>(ws + kHeaderBytes + 2 * L.buf_bytes) : nullptr;
+  p.error = a->error_word ? a->error_word : reinterpret_cast<int*>(ws) + 1;
+  uint8_t* cur = ws + kHeaderBytes;
+  p.part_cnt = L.split.cnt_bytes ? reinterpret_cast<int*>(cur) : nullptr;
+  cur += L.split.cnt_bytes;
+  p.dense_buf = L.buf_bytes ? reinterpret_cast<float*>(cur) : nullptr;
+  p.sparse_buf = L.buf_bytes ? reinterpret_cast<float*>(cur + L.buf_bytes) : nullptr;
+  cur += 2 * L.buf_bytes;
+  __nv_bfloat16* delta_buf = L.delta_bytes ? reinterpret_cast<__nv_bfloat16*>(cur) : nullptr;
   p.delta_buf = delta_buf;
+  cur += L.delta_bytes;
+  p.part_o = L.split.part_o_bytes ? reinterpret_cast<float*>(cur) : nullptr;
+  cur += L.split.part_o_bytes;
+  p.part_lse = L.split.part_lse_bytes ? reinterpret_cast<float*>(cur) : nullptr;
 
   if ((st = encode_4d(&p.tm_k, a->k, d, S, Hkv, B, a->k_stride_s, a->k_stride_h, a->k_stride_b, dta::PREFILL_BN, 1)) != DTA_OK)
     return st;
@@ -225,23 +330,25 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   if ((st = encode_4d(&p.tm_q, a->q, d, S, H, B, a->q_stride_s, a->q_stride_h, a->q_stride_b, R, G)) != DTA_OK)
     return st;
 
-  cudaError_t e = cudaMemsetAsync(a->workspace, 0, kHeaderBytes, stream);
-  if (e != cudaSuccess) return fail_cuda(e);
-
-  // With gamma = 64, uniform anchors and 4 heads per KV group, every 64-row job
-  // of the windowed launch starts at its anchor row, so that launch forms
-  // delta = dense - sparse itself from the anchor row's own sparse output and
-  // the rows launch skips the sparse anchor rows (and the delta kernel).  Both
-  // phases derive the choice from the arguments alone.
-  const bool fuse = a->mode == DTA_MODE_DELTA && !a->anchors && a->gamma == 64 && G == 4 && L.n_anchor > 0;
+  // the job counter, the workspace error word and the split counters start
+  // at zero (the ROWS phase uses them; a WINDOW-only call keeps the error word
+  // of the ROWS call before it)
+  cudaError_t e;
+  if (phases & DTA_PHASE_ROWS) {
+    e = cudaMemsetAsync(a->workspace, 0, kHeaderBytes + L.split.cnt_bytes, stream);
+    if (e != cudaSuccess) return fail_cuda(e);
+  }
+  const bool fuse = L.fuse;
   // launch 1: dense rows (anchors + tail) and, unless fused, sparse anchor rows
   if ((phases & DTA_PHASE_ROWS) && a->mode != DTA_MODE_SPARSE_ONLY && L.n_sel > 0) {
     dta::PrefillParams r = p;
     r.launch = dta::LAUNCH_ROWS;
     r.direct_from = (a->mode == DTA_MODE_DELTA) ? L.n_anchor : 0;
-    r.n_dense_tiles = (L.n_sel + JR - 1) / JR;
-    r.n_sparse_tiles = (a->mode == DTA_MODE_DELTA && !fuse) ? (L.n_anchor + JR - 1) / JR : 0;
-    r.n_jobs = (r.n_dense_tiles + r.n_sparse_tiles) * B * Hkv;
+    r.n_dense_tiles = L.split.n_dense_tiles;
+    r.n_sparse_tiles = L.n_sparse_tiles;
+    r.split_c = L.split.c;
+    r.split_cmax = L.split.cmax;
+    r.n_jobs = (r.n_dense_tiles * L.split.cmax + r.n_sparse_tiles) * B * Hkv;
     const int grid = r.n_jobs < sms ? r.n_jobs : sms;
     if ((e = dta::launch_prefill(r, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
   }
@@ -274,12 +381,13 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   return DTA_OK;
 }
 
-size_t dta_rows_workspace_size(const dta_rows_args* a) {
-  (void)a;
-  return kHeaderBytes;
-}
+}  // extern "C"
 
-int dta_rows(const dta_rows_args* a, void* stream_) {
+namespace {
+
+// Validation and split plan of dta_rows (workspace: header | split counters |
+// split partials).
+int rows_layout(const dta_rows_args* a, int sms, RowsSplit* S, size_t* ws_bytes) {
   if (!a || a->abi_version != DTA_ABI_VERSION) return DTA_ERR_INVALID_ARG;
   if (a->batch <= 0 || a->n_heads <= 0 || a->n_kv_heads <= 0 || a->seq_len <= 0 || a->n_rows <= 0 ||
       a->kv_len <= 0)
@@ -288,18 +396,51 @@ int dta_rows(const dta_rows_args* a, void* stream_) {
   if (a->n_heads % a->n_kv_heads != 0) return DTA_ERR_SHAPE;
   const int G = a->n_heads / a->n_kv_heads;
   if (G > 128 || 128 % G != 0) return DTA_ERR_SHAPE;
+  if (a->split_tiles < 0) return DTA_ERR_INVALID_ARG;
+  const int JR = dta::PREFILL_NQ * (128 / G), n = a->n_rows;
+  const long long last_key = a->kv_len - 1;
+  // key limits come from a device list: assume them spread over [0, kv_len)
+  auto tiles_of = [&](int t) {
+    const long long i = (t + 1) * (long long)JR < n ? (t + 1) * (long long)JR : n;
+    return (int)(last_key * i / n / dta::PREFILL_BN) + 1;
+  };
+  *S = plan_rows_split(a->batch * a->n_kv_heads, n, JR, a->head_dim, sms, 0, a->split_tiles, tiles_of);
+  *ws_bytes = kHeaderBytes + S->cnt_bytes + S->part_o_bytes + S->part_lse_bytes;
+  return DTA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t dta_rows_workspace_size(const dta_rows_args* a) {
+  RowsSplit S;
+  size_t bytes = 0;
+  if (rows_layout(a, sizing_sms(), &S, &bytes) != DTA_OK) return 0;
+  return bytes;
+}
+
+int dta_rows(const dta_rows_args* a, void* stream_) {
+  RowsSplit S;
+  size_t ws_bytes = 0;
+  int st = rows_layout(a, 148, &S, &ws_bytes);
+  if (st != DTA_OK) return st;
+  if (!a->workspace) return DTA_ERR_WORKSPACE;
   if (!a->q || !a->k || !a->v || !a->out || !a->q_rows || !a->kv_limit) return DTA_ERR_INVALID_ARG;
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out)) return DTA_ERR_ALIGNMENT;
   if (!stride_ok(a->q_stride_s) || !stride_ok(a->q_stride_h) || !stride_ok(a->q_stride_b) ||
       !stride_ok(a->k_stride_s) || !stride_ok(a->k_stride_h) || !stride_ok(a->k_stride_b) ||
       !stride_ok(a->v_stride_s) || !stride_ok(a->v_stride_h) || !stride_ok(a->v_stride_b))
     return DTA_ERR_STRIDE;
-  if (!a->workspace || a->workspace_bytes < kHeaderBytes || !aligned16(a->workspace)) return DTA_ERR_WORKSPACE;
-  int sms = 0, st;
+  if (a->wait_cycles < 0 || (a->flags & ~DTA_FLAG_TEST_STALL) != 0) return DTA_ERR_INVALID_ARG;
+  if (a->error_word && ((uintptr_t)a->error_word & 3u) != 0) return DTA_ERR_ALIGNMENT;
+  int sms = 0;
   if ((st = check_device(&sms)) != DTA_OK) return st;
+  if ((st = rows_layout(a, sms, &S, &ws_bytes)) != DTA_OK) return st;
+  if (a->workspace_bytes < ws_bytes || !aligned16(a->workspace)) return DTA_ERR_WORKSPACE;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  const int B = a->batch, H = a->n_heads, Hkv = a->n_kv_heads, d = a->head_dim, R = 128 / G,
-            JR = dta::PREFILL_NQ * R;
+  const int G = a->n_heads / a->n_kv_heads;
+  const int B = a->batch, H = a->n_heads, Hkv = a->n_kv_heads, d = a->head_dim, R = 128 / G;
   dta::PrefillParams p;
   memset(&p, 0, sizeof(p));
   p.q = reinterpret_cast<const __nv_bfloat16*>(a->q);
@@ -317,19 +458,31 @@ int dta_rows(const dta_rows_args* a, void* stream_) {
   p.direct_from = 0;
   p.out_by_list = 1;
   p.out_rows = a->n_rows;
+  p.seq_q = a->seq_len;
+  p.kv_len = a->kv_len;
   p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
+  p.wait_cycles = a->wait_cycles;
+  p.test_stall = (a->flags & DTA_FLAG_TEST_STALL) ? 1 : 0;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
   p.counter = reinterpret_cast<int*>(ws);
-  p.error = reinterpret_cast<int*>(ws) + 1;
-  p.n_dense_tiles = (a->n_rows + JR - 1) / JR;
-  p.n_jobs = p.n_dense_tiles * B * Hkv;
+  p.error = a->error_word ? a->error_word : reinterpret_cast<int*>(ws) + 1;
+  uint8_t* cur = ws + kHeaderBytes;
+  p.part_cnt = S.cnt_bytes ? reinterpret_cast<int*>(cur) : nullptr;
+  cur += S.cnt_bytes;
+  p.part_o = S.part_o_bytes ? reinterpret_cast<float*>(cur) : nullptr;
+  cur += S.part_o_bytes;
+  p.part_lse = S.part_lse_bytes ? reinterpret_cast<float*>(cur) : nullptr;
+  p.n_dense_tiles = S.n_dense_tiles;
+  p.split_c = S.c;
+  p.split_cmax = S.cmax;
+  p.n_jobs = p.n_dense_tiles * S.cmax * B * Hkv;
   if ((st = encode_4d(&p.tm_k, a->k, d, a->kv_len, Hkv, B, a->k_stride_s, a->k_stride_h, a->k_stride_b, dta::PREFILL_BN, 1)) !=
       DTA_OK)
     return st;
   if ((st = encode_4d(&p.tm_v, a->v, d, a->kv_len, Hkv, B, a->v_stride_s, a->v_stride_h, a->v_stride_b, dta::PREFILL_BN, 1)) !=
       DTA_OK)
     return st;
-  cudaError_t e = cudaMemsetAsync(a->workspace, 0, kHeaderBytes, stream);
+  cudaError_t e = cudaMemsetAsync(a->workspace, 0, kHeaderBytes + S.cnt_bytes, stream);
   if (e != cudaSuccess) return fail_cuda(e);
   const int grid = p.n_jobs < sms ? p.n_jobs : sms;
   if ((e = dta::launch_prefill(p, d, grid, stream)) != cudaSuccess) return fail_cuda(e);

@@ -139,6 +139,7 @@ struct Ctrl {
   uint64_t delta_ready;     // fused delta: tile A wrote this job's anchor rows (4 warps)
   uint64_t delta_free;      // fused delta: tile B read them (4 warps)
   uint64_t drain;
+  uint64_t stall;           // test hook: a barrier that nothing completes
   alignas(16) uint32_t dslot[4][64];  // fused delta: bf16 (dense - sparse) row of each head's anchor (read as uint4)
   int job[2][8];
   Plan plan[2];             // key-tile plan of job[slot], computed once by the producer
@@ -174,6 +175,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   const int lane = threadIdx.x & 31;
   volatile int* abort_flag = &ctrl->abort_flag;
   int* err = p.error;
+  const WaitCtx wc{abort_flag, err, p.wait_cycles > 0 ? p.wait_cycles : kWaitTimeoutCycles};
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -206,6 +208,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     mbar_init(BAR(delta_ready), 4);
     mbar_init(BAR(delta_free), 4);
     mbar_init(BAR(drain), 1);
+    mbar_init(BAR(stall), 1);
     ctrl->abort_flag = 0;
     mbar_init_fence();
   }
@@ -232,29 +235,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   if (warp == 0) {
     // ======================= producer =======================
     int n = 0;                // K/V tiles issued so far (ring position)
+    int nk = 0, nv = 0;       // K / V tile loads issued (for the drain on abort)
     int q_fills[NQ] = {0, 0};  // Q loads issued per slot (tile q uses slot q)
+    int fetched = 0;          // window launch: jobs taken from this CTA's static stride
     bool ok = true;
+    if (p.test_stall) {
+      // test hook: wait for a barrier phase that never completes, so this
+      // wait runs out after the budget and the CTA takes the abort path
+      ok = mbar_wait_warp(BAR(stall), 0, wc, KERR_TIMEOUT_PRODUCER);
+    }
     for (int it = 0; ok; ++it) {
       const int slot = it & 1;
-      int j;
-      if (p.launch == LAUNCH_WINDOW) {
-        j = blockIdx.x + it * gridDim.x;
-      } else {
-        int jj = 0;
-        if (lane == 0) jj = atomicAdd(p.counter, 1);
-        j = __shfl_sync(0xffffffffu, jj, 0);
+      // the plan goes out with the job: the consumers would otherwise each
+      // run make_plan, cold code on their critical path at every job change.
+      // Chunk slots past a short row tile's chunks are empty and skipped here.
+      Job J;
+      Plan P{};
+      for (;;) {
+        int j;
+        if (p.launch == LAUNCH_WINDOW) {
+          j = blockIdx.x + (fetched++) * gridDim.x;
+        } else {
+          int jj = 0;
+          if (lane == 0) jj = atomicAdd(p.counter, 1);
+          j = __shfl_sync(0xffffffffu, jj, 0);
+        }
+        J = decode_job(p, j);
+        if (J.kind == JOB_END) break;
+        P = make_plan(p, J);
+        if (P.n_tiles > 0) break;
       }
-      if (!mbar_wait_warp(BAR(job_empty[0]) + 8 * slot, ((it >> 1) & 1) ^ 1, abort_flag, err,
+      if (!mbar_wait_warp(BAR(job_empty[0]) + 8 * slot, ((it >> 1) & 1) ^ 1, wc,
                           KERR_TIMEOUT_PRODUCER))
         break;
-      const Job J = decode_job(p, j);
-      // the plan goes out with the job: the consumers would otherwise each
-      // run make_plan, cold code on their critical path at every job change
-      Plan P{};
-      if (J.kind != JOB_END) P = make_plan(p, J);
       if (lane == 0) {
         int* dst = ctrl->job[slot];
-        dst[0] = J.kind; dst[1] = J.b; dst[2] = J.g; dst[3] = J.start; dst[4] = J.count;
+        dst[0] = J.kind; dst[1] = J.b; dst[2] = J.g; dst[3] = J.start; dst[4] = J.count; dst[5] = J.chunk;
         if (J.kind != JOB_END) ctrl->plan[slot] = P;
         mbar_arrive(BAR(job_full[0]) + 8 * slot);  // release: job and plan are visible to the waiters
       }
@@ -267,7 +283,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         constexpr int q = decltype(qc)::value, qs = q;
         if (P.tiles_t[q] == 0) return true;
         const uint32_t qbuf = q_u32 + (uint32_t)qs * G::TILE_BYTES;
-        if (!mbar_wait_warp(BAR(q_empty[0]) + 8 * qs, (q_fills[qs] & 1) ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER))
+        if (!mbar_wait_warp(BAR(q_empty[0]) + 8 * qs, (q_fills[qs] & 1) ^ 1, wc, KERR_TIMEOUT_PRODUCER))
           return false;
         ++q_fills[qs];
         if (J.kind == JOB_WINDOW) {
@@ -288,7 +304,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
             const int hh = m >> r_shift, rr = m & (p.R - 1);
             const int li = q * p.R + rr;
             const bool valid = li < J.count;
-            const int row = valid ? list_q_row(p, J.start + li) : 0;
+            const int row = valid ? clamp_row(p, list_q_row(p, J.start + li), p.seq_q) : 0;
             const __nv_bfloat16* src =
                 qb + (long long)(J.g * p.G + hh) * p.q_sh + (long long)row * p.q_ss + cc * 8;
             const int region = cc >> 3, cw = cc & 7;
@@ -308,7 +324,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         const int st = n % G::K_STAGES, sv = n % G::V_STAGES;
         const uint32_t ph = (uint32_t)((n / G::K_STAGES) & 1), phv = (uint32_t)((n / G::V_STAGES) & 1);
         const int ks = tile_key_start(P, i);
-        if (!mbar_wait_warp(BAR(k_empty[0]) + 8 * st, ph ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER)) {
+        if (!mbar_wait_warp(BAR(k_empty[0]) + 8 * st, ph ^ 1, wc, KERR_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
         }
@@ -318,7 +334,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           for (int r = 0; r < G::REGIONS; ++r)
             tma_load_4d(kdst + r * G::KV_REGION_BYTES, &p.tm_k, BAR(k_full[0]) + 8 * st, r * 64, ks, J.g, J.b);
         }
-        if (!mbar_wait_warp(BAR(v_empty[0]) + 8 * sv, phv ^ 1, abort_flag, err, KERR_TIMEOUT_PRODUCER)) {
+        nk = n + 1;
+        if (!mbar_wait_warp(BAR(v_empty[0]) + 8 * sv, phv ^ 1, wc, KERR_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
         }
@@ -328,22 +345,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           for (int r = 0; r < G::REGIONS; ++r)
             tma_load_4d(vdst + r * G::KV_REGION_BYTES, &p.tm_v, BAR(v_full[0]) + 8 * sv, r * 64, ks, J.g, J.b);
         }
+        nv = n + 1;
         if (i == 0 && !load_q(std::integral_constant<int, 0>{})) {
           ok = false;
           break;
         }
       }
     }
-    // On abort, let in-flight TMA loads land before the CTA can exit.
+    // On abort, let in-flight TMA loads land before the CTA can exit: at most
+    // the last K_STAGES K loads, V_STAGES V loads and one Q load per slot can
+    // still be in flight (each load waited for its stage to be consumed).
     if (*abort_flag && lane == 0) {
-      for (int m = max(0, n - (G::K_STAGES > G::V_STAGES ? G::K_STAGES : G::V_STAGES)); m < n; ++m) {
-        const int st = m % G::K_STAGES, sv = m % G::V_STAGES;
-        const uint32_t ph = (uint32_t)((m / G::K_STAGES) & 1), phv = (uint32_t)((m / G::V_STAGES) & 1);
+      auto drain = [](uint32_t bar, uint32_t parity) {
         const long long t0 = clock64();
-        while (!(mbar_try_wait(BAR(k_full[0]) + 8 * st, ph) && mbar_try_wait(BAR(v_full[0]) + 8 * sv, phv))) {
+        while (!mbar_try_wait(bar, parity))
           if (clock64() - t0 > kWaitTimeoutCycles) break;
-        }
-      }
+      };
+      for (int m = max(0, nk - G::K_STAGES); m < nk; ++m)
+        drain(BAR(k_full[0]) + 8 * (m % G::K_STAGES), (uint32_t)((m / G::K_STAGES) & 1));
+      for (int m = max(0, nv - G::V_STAGES); m < nv; ++m)
+        drain(BAR(v_full[0]) + 8 * (m % G::V_STAGES), (uint32_t)((m / G::V_STAGES) & 1));
+      if (q_fills[0] > 0) drain(BAR(q_full[0]), (uint32_t)((q_fills[0] - 1) & 1));
+      if (q_fills[1] > 0) drain(BAR(q_full[0]) + 8, (uint32_t)((q_fills[1] - 1) & 1));
     }
   } else if (warp == 1) {
     // ======================= MMA issuer =======================
@@ -369,7 +392,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       bool aborted = false;
       for (int it = 0; !aborted; ++it) {
         const int slot = it & 1;
-        if (!mbar_poll(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA)) break;
+        if (!mbar_poll(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, wc, KERR_TIMEOUT_MMA)) break;
         Job J;
         {
           const volatile int* src = ctrl->job[slot];
@@ -386,11 +409,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           constexpr int q = decltype(qc)::value;
           const int m = n0 + i, st = m % G::K_STAGES;
           if (i == 0) {
-            if (!mbar_poll(BAR(q_full[0]) + 8 * q, q_uses[q] & 1, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
+            if (!mbar_poll(BAR(q_full[0]) + 8 * q, q_uses[q] & 1, wc, KERR_TIMEOUT_MMA)) return false;
             ++q_uses[q];
           }
           if (q == 0 || i >= tiles[0]) {  // first user of K_i waits for it
-            if (!mbar_poll(BAR(k_full[0]) + 8 * st, (m / G::K_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+            if (!mbar_poll(BAR(k_full[0]) + 8 * st, (m / G::K_STAGES) & 1, wc, KERR_TIMEOUT_MMA))
               return false;
           }
           tc_fence_after();
@@ -420,13 +443,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           const int m = n0 + i, st = m % G::V_STAGES;
           const uint32_t pbar = BAR(p_full[0]) + 8 * (2 * q);
           const uint32_t pph = (uint32_t)(cnt_pv[q] & 1);
-          if (!mbar_poll(pbar, pph, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
+          if (!mbar_poll(pbar, pph, wc, KERR_TIMEOUT_MMA)) return false;
           if (i == 0 && jobs_t[q] > 0) {
-            if (!mbar_poll(BAR(o_empty[0]) + 8 * q, (jobs_t[q] - 1) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+            if (!mbar_poll(BAR(o_empty[0]) + 8 * q, (jobs_t[q] - 1) & 1, wc, KERR_TIMEOUT_MMA))
               return false;
           }
           if (q == 0 || i >= tiles[0]) {  // first user of V_i waits for it
-            if (!mbar_poll(BAR(v_full[0]) + 8 * st, (m / G::V_STAGES) & 1, abort_flag, err, KERR_TIMEOUT_MMA))
+            if (!mbar_poll(BAR(v_full[0]) + 8 * st, (m / G::V_STAGES) & 1, wc, KERR_TIMEOUT_MMA))
               return false;
           }
           tc_fence_after();
@@ -439,7 +462,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
               umma_ts(tO, tP + kk * 8, vd + ((kk * 2048) >> 4), IDESC_PV, (i == 0 && kk == 0) ? 0u : 1u);
           }
           __syncwarp();
-          if (!mbar_poll(pbar + 8, pph, abort_flag, err, KERR_TIMEOUT_MMA)) return false;
+          if (!mbar_poll(pbar + 8, pph, wc, KERR_TIMEOUT_MMA)) return false;
           tc_fence_after();
           if (elect_one()) {
 #pragma unroll
@@ -506,7 +529,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     int f_reads = 0;    // fused delta: of those, read by tile B
     for (int it = 0;; ++it) {
       const int slot = it & 1;
-      if (!mbar_wait_warp(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
+      if (!mbar_wait_warp(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, wc, KERR_TIMEOUT_SOFTMAX)) break;
       Job J;
       {
         const volatile int* src = ctrl->job[slot];
@@ -556,7 +579,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       float m_run = -INFINITY, l_run = 0.f;
       bool aborted = false;
       for (int i = 0; i < T; ++i, ++cnt) {
-        if (!mbar_wait_warp(BAR(s_full[0]) + 8 * q, cnt & 1, abort_flag, err,
+        if (!mbar_wait_warp(BAR(s_full[0]) + 8 * q, cnt & 1, wc,
                             KERR_TIMEOUT_SOFTMAX)) {
           aborted = true;
           break;
@@ -710,20 +733,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           mode_out = 1;
         } else {
           out_row = !row_valid ? 0 : (p.out_by_list ? gli : list_q_row(p, gli));
+          if (out_row < 0 || out_row >= p.out_rows) {  // a bad explicit anchor: flagged, not stored
+            if (store) atomicCAS(p.error, 0, KERR_BAD_ROW);
+            store = false;
+          }
         }
       } else {
         mode_out = 2;
       }
       // 1/l to ~2 ulp (__fdividef): far below the bf16 rounding of the output
       const float inv_l = (l_run > 0.f) ? __fdividef(1.f, l_run) : 0.f;
-      const uint64_t inv2 = f2_pack(inv_l, inv_l);
-      __nv_bfloat16* dst_bf = (store && mode_out == 0)
-                                  ? p.out + (((long long)J.b * p.out_rows + out_row) * p.H + h) * HD
-                                  : nullptr;
-      float* dst_f = (store && mode_out != 0)
-                         ? (mode_out == 1 ? p.dense_buf : p.sparse_buf) +
-                               (((long long)J.b * p.n_anchor + gli) * p.H + h) * HD
-                         : nullptr;
       // (fused delta, tile A: this lane's 4 columns of the anchor's dense row,
       // loaded while the last PV runs)
       const float4 dn4 = (fuse && q == 0)
@@ -731,7 +750,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
                              : make_float4(0.f, 0.f, 0.f, 0.f);
       // o_full[q] completes once per job of this tile (after its last PV); the
       // next job's first PV waits for o_empty[q], so phases cannot run ahead
-      if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, jobs_done & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) break;
+      if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, jobs_done & 1, wc, KERR_TIMEOUT_SOFTMAX)) break;
       tc_fence_after();
       float o[HD];
 #pragma unroll
@@ -741,6 +760,95 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(o_empty[0]) + 8 * q);
       ++jobs_done;
+      if (J.kind == JOB_DENSE_ROWS && P.n_chunks > 1) {
+        // ---- split dense job: store this chunk's partial (O / l and the
+        // log2-sum-exp of every row); the chunk that finishes last merges all
+        // of them and stores the rows ----
+        const int r_shift = __ffs(p.R) - 1;
+        const long long tile_id = (long long)(J.b * p.Hkv + J.g) * p.n_dense_tiles + (J.start >> (r_shift + 1));
+        const int act = q ? P.act_t[1] : P.act_t[0];
+        auto slot_of = [&](int k) { return ((tile_id * p.split_cmax + k) * NQ + q) * 128; };
+        const float lse = (l_run > 0.f) ? m_run + __log2f(l_run) : -INFINITY;
+        {
+          float4* po = reinterpret_cast<float4*>(p.part_o) + slot_of(P.chunk) * (HD / 4) + r;
+#pragma unroll
+          for (int c4 = 0; c4 < HD / 4; ++c4)
+            po[c4 * 128] = make_float4(o[4 * c4] * inv_l, o[4 * c4 + 1] * inv_l, o[4 * c4 + 2] * inv_l,
+                                       o[4 * c4 + 3] * inv_l);
+          p.part_lse[slot_of(P.chunk) + r] = lse;
+        }
+        // Each warp counts its own 32 rows' chunks (no barrier across the
+        // warpgroup, whose warps may leave the job loop independently on an
+        // abort): every lane's partial is visible device-wide before lane 0
+        // moves the count.
+        __threadfence();
+        __syncwarp();
+        int done = 0;
+        if (lane == 0) done = atomicAdd(p.part_cnt + (tile_id * NQ + q) * 4 + quarter, 1);
+        done = __shfl_sync(0xffffffffu, done, 0);
+        if (done != act - 1) continue;  // another chunk merges these rows
+        __threadfence();
+        // Last chunk: log-sum-exp merge of the tile's active chunks, read back
+        // from L2 (bypassing L1) 32 columns at a time, so this thread's own O
+        // is no longer needed in registers; the rows are stored from here.
+        float M = -INFINITY;
+        for (int k = 0; k < act; ++k) M = fmaxf(M, __ldcg(p.part_lse + slot_of(k) + r));
+        float wsum = 0.f;
+        for (int k = 0; k < act; ++k) {
+          const float lk = __ldcg(p.part_lse + slot_of(k) + r);
+          wsum += (lk == -INFINITY) ? 0.f : fast_exp2(lk - M);
+        }
+        const float inv_w = (wsum > 0.f) ? __fdividef(1.f, wsum) : 0.f;
+        __nv_bfloat16* dbf = (store && mode_out == 0)
+                                 ? p.out + (((long long)J.b * p.out_rows + out_row) * p.H + h) * HD
+                                 : nullptr;
+        float* dfl = (store && mode_out == 1) ? p.dense_buf + (((long long)J.b * p.n_anchor + gli) * p.H + h) * HD
+                                              : nullptr;
+#pragma unroll 1
+        for (int cb = 0; cb < HD / 32; ++cb) {
+          float acc[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+          for (int k = 0; k < act; ++k) {
+            const float lk = __ldcg(p.part_lse + slot_of(k) + r);
+            const float w = (lk == -INFINITY) ? 0.f : fast_exp2(lk - M) * inv_w;
+            const float4* pk = reinterpret_cast<const float4*>(p.part_o) + slot_of(k) * (HD / 4) + cb * 8 * 128 + r;
+            float4 v4[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v4[u] = __ldcg(pk + u * 128);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              acc[4 * u] = fmaf(w, v4[u].x, acc[4 * u]);
+              acc[4 * u + 1] = fmaf(w, v4[u].y, acc[4 * u + 1]);
+              acc[4 * u + 2] = fmaf(w, v4[u].z, acc[4 * u + 2]);
+              acc[4 * u + 3] = fmaf(w, v4[u].w, acc[4 * u + 3]);
+            }
+          }
+          if (dfl) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              reinterpret_cast<float4*>(dfl + cb * 32)[u] =
+                  make_float4(acc[4 * u], acc[4 * u + 1], acc[4 * u + 2], acc[4 * u + 3]);
+          } else if (dbf) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 16) {
+              uint32_t w8[8];
+#pragma unroll
+              for (int k2 = 0; k2 < 8; ++k2) w8[k2] = pack_bf16x2(acc[e + 2 * k2], acc[e + 2 * k2 + 1]);
+              st_global_v8(dbf + cb * 32 + e, w8);
+            }
+          }
+        }
+        continue;
+      }
+      const uint64_t inv2 = f2_pack(inv_l, inv_l);
+      __nv_bfloat16* dst_bf = (store && mode_out == 0)
+                                  ? p.out + (((long long)J.b * p.out_rows + out_row) * p.H + h) * HD
+                                  : nullptr;
+      float* dst_f = (store && mode_out != 0)
+                         ? (mode_out == 1 ? p.dense_buf : p.sparse_buf) +
+                               (((long long)J.b * p.n_anchor + gli) * p.H + h) * HD
+                         : nullptr;
       // this tile's staging half is free once its last store has read it (the
       // leader waits for that store only now, so it never holds up the warps)
       const uint32_t half = base_u32 + G::STG_OFF + q * G::STG_HALF;
@@ -751,7 +859,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           st_pending = false;
         }
         if (st_rounds > 0 &&
-            !mbar_wait_warp(BAR(stg_free[0]) + 8 * q, (st_rounds - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX))
+            !mbar_wait_warp(BAR(stg_free[0]) + 8 * q, (st_rounds - 1) & 1, wc, KERR_TIMEOUT_SOFTMAX))
           break;
       }
       // the anchor's bf16 delta row: global (dlt) or, fused, this head's slot
@@ -760,7 +868,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         if (q == 0) {
           // the slot is free once tile B has read the previous job's rows
           if (f_reads_prev > 0 &&
-              !mbar_wait_warp(BAR(delta_free), (f_reads_prev - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX))
+              !mbar_wait_warp(BAR(delta_free), (f_reads_prev - 1) & 1, wc, KERR_TIMEOUT_SOFTMAX))
             break;
           // lane 0's row is the anchor (position J.start).  Its raw O row goes
           // through the first 512 bytes of this warp's own staging rows; each
@@ -784,7 +892,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           }
           __syncwarp();  // the slot is complete and the staging rows may be overwritten
           if (lane == 0) mbar_arrive(BAR(delta_ready));
-        } else if (!mbar_wait_warp(BAR(delta_ready), f_writes_prev & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
+        } else if (!mbar_wait_warp(BAR(delta_ready), f_writes_prev & 1, wc, KERR_TIMEOUT_SOFTMAX)) {
           break;
         }
         dsrc = reinterpret_cast<const uint4*>(&ctrl->dslot[quarter][0]);
@@ -797,7 +905,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
 #pragma unroll
         for (int rg = 0; rg < G::REGIONS; ++rg) {
           if (rg > 0 &&
-              !mbar_wait_warp(BAR(stg_free[0]) + 8 * q, (st_rounds - 1) & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX)) {
+              !mbar_wait_warp(BAR(stg_free[0]) + 8 * q, (st_rounds - 1) & 1, wc, KERR_TIMEOUT_SOFTMAX)) {
             ok = false;
             break;
           }
@@ -824,7 +932,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
             // leader: once all four warps wrote their rows, store the round; the
             // half is released when the store has read it (for the tile's last
             // round, at this tile's next use)
-            ok = mbar_wait(BAR(stg_full[0]) + 8 * q, st_rounds & 1, abort_flag, err, KERR_TIMEOUT_SOFTMAX);
+            ok = mbar_wait(BAR(stg_full[0]) + 8 * q, st_rounds & 1, wc, KERR_TIMEOUT_SOFTMAX);
             if (ok) {
               tma_store_4d(&p.tm_out, half, rg * 64, J.start + q * p.R, J.g * p.G, J.b);
               bulk_commit_group();

@@ -55,6 +55,21 @@ struct PrefillParams {
   float* anchor_delta_f32;      // optional fp32 dense - sparse per anchor (telemetry)
   __nv_bfloat16* out;           // [B, out_rows, H, d]
   int tma_out;                  // window launch: full tiles leave through tm_out (TMA stores)
+  // Split-K of the rows launch's dense jobs.  A dense job (one row tile of the
+  // list) whose key range spans T tiles runs as c = min(ceil(T / split_c),
+  // split_cmax) jobs ("chunks") over equal key ranges; each chunk stores its
+  // rows' O / l and log2-sum-exp as partials, and the chunk that finishes last
+  // (per query tile and warp, counted in part_cnt) merges them and stores the
+  // rows.  split_c == 0: no split (one chunk per row tile).  The job index
+  // space reserves split_cmax chunks per row tile; chunks past a short tile's
+  // c are skipped by the producer.
+  int split_c, split_cmax;
+  float* part_o;                // [B*Hkv][n_dense_tiles][split_cmax][NQ][d/4][128] float4
+  float* part_lse;              // [B*Hkv][n_dense_tiles][split_cmax][NQ][128]
+  int* part_cnt;                // [B*Hkv][n_dense_tiles][NQ][4 warps] chunks finished, zeroed by the host
+  long long wait_cycles;        // budget of each bounded wait (clock64 cycles)
+  int test_stall;               // test hook: the producer first waits on a barrier nothing completes
+  int seq_q, kv_len;            // rows of q and of k/v: bounds for explicit row lists
 };
 
 // Multiplier and shift with n / d == (n * mul) >> sh for every 0 <= n < 2^31

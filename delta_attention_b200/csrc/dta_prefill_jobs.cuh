@@ -1,8 +1,9 @@
-// Jobs and key-tile plans of the prefill kernels (device code shared by both
-// kernel variants; identical in every role of a kernel).
+// Jobs and key-tile plans of the prefill kernel (device code identical in
+// every role of the kernel).
 #pragma once
 
 #include "dta_prefill.h"
+#include "dta_ptx.cuh"
 
 namespace dta {
 
@@ -10,24 +11,38 @@ enum JobKind : int { JOB_END = -1, JOB_WINDOW = 0, JOB_DENSE_ROWS = 1, JOB_SPARS
 
 struct Job {
   int kind, b, g, start, count;
+  int chunk;  // dense row jobs: key-range chunk of the row tile
 };
 
 // ---------------------------------------------------------------------------
 // row lists, jobs and key-tile plans (identical in every role)
 // ---------------------------------------------------------------------------
+// A list entry outside the tensors is recorded in the error word and clamped,
+// so a bad caller array costs a wrong (flagged) output, never a stray access.
+__device__ __forceinline__ int clamp_row(const PrefillParams& p, int row, int n) {
+  if (row < 0 || row >= n) {
+    atomicCAS(p.error, 0, KERR_BAD_ROW);
+    row = min(max(row, 0), n - 1);
+  }
+  return row;
+}
 __device__ __forceinline__ int list_q_row(const PrefillParams& p, int i) {
   if (p.q_rows) return p.q_rows[i];
   if (i < p.n_anchor) return p.anchors ? p.anchors[i] : i * p.gamma;
   return p.s_p + (i - p.n_anchor);
 }
 __device__ __forceinline__ int list_kv_limit(const PrefillParams& p, int i) {
-  if (p.kv_limit) return p.kv_limit[i];
-  return list_q_row(p, i);
+  return clamp_row(p, p.kv_limit ? p.kv_limit[i] : list_q_row(p, i), p.kv_len);
 }
 
+// Job index -> job.  Window launch: (batch x group)-major R*NQ-row tiles of
+// rows [0, row_end).  Rows launch: dense row tiles longest first (each with
+// split_cmax chunk slots), then sparse anchor tiles; the batch x group index
+// varies fastest.
 static __device__ Job decode_job(const PrefillParams& p, int j) {
   Job J;
   const int JR = PREFILL_NQ * p.R;  // rows per job
+  J.chunk = 0;
   if (j >= p.n_jobs) {
     J.kind = JOB_END;
     J.b = J.g = J.start = J.count = 0;
@@ -44,16 +59,19 @@ static __device__ Job decode_job(const PrefillParams& p, int j) {
     return J;
   }
   const int BG = p.B * p.Hkv;
-  const int rank = j / BG, bg = j - (j / BG) * BG;
+  const int u = j / BG, bg = j - (j / BG) * BG;
   J.b = bg / p.Hkv;
   J.g = bg - J.b * p.Hkv;
-  if (rank < p.n_dense_tiles) {
+  const int cmax = p.split_cmax > 0 ? p.split_cmax : 1;
+  if (u < p.n_dense_tiles * cmax) {
+    const int rank = u / cmax;
     const int tile = p.n_dense_tiles - 1 - rank;  // longest (latest rows) first
     J.kind = JOB_DENSE_ROWS;
+    J.chunk = u - rank * cmax;
     J.start = tile * JR;
     J.count = min(JR, p.n_sel - J.start);
   } else {
-    const int tile = rank - p.n_dense_tiles;
+    const int tile = u - p.n_dense_tiles * cmax;
     J.kind = JOB_SPARSE_ROWS;
     J.start = tile * JR;
     J.count = min(JR, p.n_anchor - J.start);
@@ -88,11 +106,14 @@ __device__ __forceinline__ int block_window_lo(const PrefillParams& p, int t) {
 }
 
 // Key tiles of a job: sink segment [0, sink_end) then window segment
-// [lo_min, qmax]; dense jobs have only [0, qmax].  Query tile q takes the
-// prefix of tiles whose first key is <= the tile's last row.
+// [lo_min, qmax]; dense jobs have the one segment [lo_min, ...) of their
+// chunk (lo_min = 0 when unsplit).  Query tile q takes the prefix of tiles
+// whose first key is <= the tile's last row.
 struct Plan {
   int n0, n_tiles, sink_end, lo_min, qmax;
+  int chunk, n_chunks;  // dense jobs: this chunk and the row tile's chunk count
   int qmin_t[PREFILL_NQ], qmax_t[PREFILL_NQ], lo_max_t[PREFILL_NQ], tiles_t[PREFILL_NQ];
+  int act_t[PREFILL_NQ];  // dense jobs: chunks in which query tile q has keys (a prefix)
 };
 
 __device__ __forceinline__ int tile_key_start(const Plan& P, int i) {
@@ -104,8 +125,11 @@ static __device__ Plan make_plan(const PrefillParams& p, const Job& J) {
   const bool dense = (J.kind == JOB_DENSE_ROWS);
   int first = -1;
   P.qmax = 0;
+  P.chunk = J.chunk;
+  P.n_chunks = 1;
 #pragma unroll
   for (int q = 0; q < PREFILL_NQ; ++q) {
+    P.act_t[q] = 1;
     const int r0 = q * p.R;
     const int r1 = min(J.count, (q + 1) * p.R) - 1;
     if (r1 < r0) {
@@ -121,21 +145,49 @@ static __device__ Plan make_plan(const PrefillParams& p, const Job& J) {
     P.qmax = max(P.qmax, P.qmax_t[q]);
   }
   if (dense) {
+    // key tiles [kb, ke) of this chunk out of the row tile's T
+    const int T = P.qmax / PREFILL_BN + 1;
+    int c = 1, kb = 0, ke = T;
+    if (p.split_c > 0) {
+      c = min((T + p.split_c - 1) / p.split_c, p.split_cmax);
+      kb = (int)((long long)J.chunk * T / c);
+      ke = (int)((long long)(J.chunk + 1) * T / c);
+    }
+    P.n_chunks = c;
     P.n0 = 0;
     P.sink_end = 0;
-    P.lo_min = 0;
-    P.n_tiles = P.qmax / PREFILL_BN + 1;
-  } else {
-    P.lo_min = block_window_lo(p, first);
-    P.sink_end = min(p.sink, P.lo_min);
-    P.n0 = (P.sink_end + PREFILL_BN - 1) / PREFILL_BN;
-    P.n_tiles = P.n0 + (P.qmax - P.lo_min) / PREFILL_BN + 1;
+    if (J.chunk >= c) {
+      // a chunk slot past this (short) row tile's chunks: an empty job
+      P.lo_min = 0;
+      P.n_tiles = 0;
+#pragma unroll
+      for (int q = 0; q < PREFILL_NQ; ++q) P.tiles_t[q] = 0;
+      return P;
+    }
+    P.lo_min = kb * PREFILL_BN;
+    P.n_tiles = ke - kb;
+#pragma unroll
+    for (int q = 0; q < PREFILL_NQ; ++q) {
+      const int m = P.qmax_t[q];
+      if (m < 0) {
+        P.tiles_t[q] = 0;
+        continue;
+      }
+      const int Tq = m / PREFILL_BN + 1;
+      P.tiles_t[q] = min(max(Tq - kb, 0), ke - kb);
+      // chunk k' has keys for tile q iff floor(k' T / c) < Tq, i.e. k' < Tq c / T
+      P.act_t[q] = min(c, (int)(((long long)Tq * c + T - 1) / T));
+    }
+    return P;
   }
+  P.lo_min = block_window_lo(p, first);
+  P.sink_end = min(p.sink, P.lo_min);
+  P.n0 = (P.sink_end + PREFILL_BN - 1) / PREFILL_BN;
+  P.n_tiles = P.n0 + (P.qmax - P.lo_min) / PREFILL_BN + 1;
 #pragma unroll
   for (int q = 0; q < PREFILL_NQ; ++q) {
     const int m = P.qmax_t[q];
     if (m < 0) P.tiles_t[q] = 0;
-    else if (dense) P.tiles_t[q] = m / PREFILL_BN + 1;
     else if (m >= P.lo_min) P.tiles_t[q] = P.n0 + (m - P.lo_min) / PREFILL_BN + 1;
     else P.tiles_t[q] = min(P.n0, m / PREFILL_BN + 1);
   }

@@ -21,11 +21,14 @@ enum : int {
   KERR_TIMEOUT_MMA = 102,
   KERR_TIMEOUT_SOFTMAX = 103,
   KERR_TIMEOUT_DRAIN = 104,
+  KERR_BAD_ROW = 105,  // a query row or key limit outside the tensors (clamped, output not trusted)
 };
 
-// ~2 s at 1.9 GHz: longer than any legitimate wait in these kernels (one
-// key tile of one job is microseconds), short enough that a broken pipeline
-// returns control to the host instead of hanging the GPU.
+// Default wait budget, ~2 s at 1.9 GHz: longer than any legitimate wait in
+// these kernels (one key tile of one job is microseconds), short enough that a
+// broken pipeline returns control to the host instead of hanging the GPU.  The
+// caller may pass a different budget; waits that drain in-flight copies or
+// tensor-core ops on the way out always use this one.
 constexpr long long kWaitTimeoutCycles = 4000000000LL;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -60,17 +63,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-static __device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                            int* err, int code) {
+// Where a bounded wait records that it gave up: the CTA's abort flag (shared
+// memory, seen by every role), the kernel error word (global memory, read by
+// the host) and the wait budget in clock64 cycles.
+struct WaitCtx {
+  volatile int* abort_flag;
+  int* err;
+  long long limit;
+};
+
+static __device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, const WaitCtx& w, int code) {
   long long t0 = clock64();
   uint32_t it = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((++it & 255u) == 0u) {
-      if (*abort_flag) return false;
-      if (clock64() - t0 > kWaitTimeoutCycles) {
-        *abort_flag = 1;
-        atomicCAS(err, 0, code);
+      if (*w.abort_flag) return false;
+      if (clock64() - t0 > w.limit) {
+        *w.abort_flag = 1;
+        atomicCAS(w.err, 0, code);
         return false;
       }
     }
@@ -78,12 +89,11 @@ static __device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t par
 }
 
 // Bounded wait for the phase with parity `parity` to complete.  Returns false
-// (after raising the CTA abort flag and recording `code` in *err) when the
-// wait exceeds kWaitTimeoutCycles, or when another role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err, int code) {
+// (after raising the CTA abort flag and recording `code` in the error word)
+// when the wait exceeds the budget, or when another role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtx& w, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  return mbar_wait_slow(bar, parity, abort_flag, err, code);
+  return mbar_wait_slow(bar, parity, w, code);
 }
 
 // Polling variant for latency-critical single-thread waiters (the MMA issuer):
@@ -101,34 +111,31 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-static __device__ __forceinline__ bool mbar_poll_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                                   int* err, int code) {
+static __device__ __forceinline__ bool mbar_poll_slow(uint32_t bar, uint32_t parity, const WaitCtx& w, int code) {
   const long long t0 = clock64();
   uint32_t it = 0;
   while (true) {
     if (mbar_test(bar, parity)) return true;
     if ((++it & 1023u) == 0u) {
-      if (*abort_flag) return false;
-      if (clock64() - t0 > kWaitTimeoutCycles) {
-        *abort_flag = 1;
-        atomicCAS(err, 0, code);
+      if (*w.abort_flag) return false;
+      if (clock64() - t0 > w.limit) {
+        *w.abort_flag = 1;
+        atomicCAS(w.err, 0, code);
         return false;
       }
     }
   }
 }
-__device__ __forceinline__ bool mbar_poll(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
-                                          int code) {
+__device__ __forceinline__ bool mbar_poll(uint32_t bar, uint32_t parity, const WaitCtx& w, int code) {
   if (mbar_test(bar, parity)) return true;
-  return mbar_poll_slow(bar, parity, abort_flag, err, code);
+  return mbar_poll_slow(bar, parity, w, code);
 }
 
 // Warp-collective variant: every lane waits, then the warp reconverges so the
 // caller may issue .sync.aligned tcgen05 instructions.  The result is the
 // AND over the warp (an abort seen by any lane aborts the whole warp).
-__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                               int* err, int code) {
-  const bool ok = mbar_wait(bar, parity, abort_flag, err, code);
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, const WaitCtx& w, int code) {
+  const bool ok = mbar_wait(bar, parity, w, code);
   return __all_sync(0xffffffffu, ok);
 }
 

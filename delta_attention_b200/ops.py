@@ -3,6 +3,13 @@
 Each op checks its inputs, sizes the caller-side workspace with the library's
 ``*_workspace_size`` query, passes raw pointers plus the current CUDA stream,
 and raises :class:`DtaError` for any non-zero status.  There is no CPU path.
+
+Kernel-side failures (a bounded wait that ran out, a row index outside the
+tensors) cannot be returned by an asynchronous launch.  Every prefill and rows
+launch therefore records them in one persistent int32 "error word" per device,
+which stays set until :func:`check_errors` reads it (at a point where the
+caller synchronises anyway) and raises ``DtaError(DTA_ERR_KERNEL_TIMEOUT)``.
+``check=True`` on an op does that right after the launch.
 """
 
 from __future__ import annotations
@@ -13,7 +20,62 @@ from typing import Optional, Tuple
 import torch
 
 from . import _lib
-from ._lib import ABI_VERSION, DecodeArgs, PrefillArgs, RowsArgs, check, lib
+from ._lib import ABI_VERSION, KERNEL_CODES, DecodeArgs, DtaError, PrefillArgs, RowsArgs, lib
+from ._lib import check as _check_status
+
+DTA_ERR_KERNEL_TIMEOUT = 10
+
+_error_words = {}
+
+
+def _device_index(device=None) -> int:
+    if device is None:
+        return torch.cuda.current_device()
+    d = torch.device(device)
+    return d.index if d.index is not None else torch.cuda.current_device()
+
+
+def error_word(device=None) -> torch.Tensor:
+    """The persistent device int32 that this device's kernels report into."""
+    idx = _device_index(device)
+    w = _error_words.get(idx)
+    if w is None:
+        w = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", idx))
+        _error_words[idx] = w
+    return w
+
+
+def check_errors(device=None) -> None:
+    """Synchronise the current stream, read this device's error word and raise
+    ``DtaError`` (status DTA_ERR_KERNEL_TIMEOUT) if any launch since the last
+    check recorded a kernel code; the word is cleared either way."""
+    w = error_word(device)
+    code = int(w[0].item())  # synchronises with the current stream
+    if code != 0:
+        w.zero_()
+        raise DtaError(DTA_ERR_KERNEL_TIMEOUT, "kernel error word",
+                       f"code {code}: {KERNEL_CODES.get(code, 'unknown')}")
+
+
+def _validate_anchors(anchors: torch.Tensor, s_p: int, s: int) -> None:
+    a = anchors.detach().to("cpu", torch.int64)
+    if a.numel() == 0 or not 0 < s_p <= s:
+        raise ValueError(f"need at least one anchor and 0 < s_p <= seq_len (s_p={s_p}, seq_len={s})")
+    if int(a[0]) != 0 or int(a[-1]) >= s_p or (a.numel() > 1 and not bool((a[1:] > a[:-1]).all())):
+        raise ValueError("anchors must start at 0, be strictly increasing and lie below s_p")
+
+
+def _validate_rows(q_rows: torch.Tensor, kv_limit: torch.Tensor, seq_len: int, kv_len: int) -> None:
+    r = q_rows.detach().to("cpu", torch.int64)
+    lim = kv_limit.detach().to("cpu", torch.int64)
+    if r.shape != lim.shape:
+        raise ValueError("q_rows and kv_limit must have the same length")
+    if bool((r < 0).any()) or bool((r >= seq_len).any()):
+        raise ValueError(f"q_rows must lie in [0, {seq_len})")
+    if bool((lim < 0).any()) or bool((lim >= kv_len).any()):
+        raise ValueError(f"kv_limit must lie in [0, {kv_len})")
+    if lim.numel() > 1 and not bool((lim[1:] >= lim[:-1]).all()):
+        raise ValueError("kv_limit must be non-decreasing")
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -57,13 +119,21 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
             scaling: Optional[float] = None, mode: str = "delta", q_block: int = 64,
             anchors: Optional[torch.Tensor] = None, s_p: Optional[int] = None,
             return_anchor_delta: bool = False, workspace: Optional[torch.Tensor] = None,
-            phases: int = 0, out: Optional[torch.Tensor] = None):
+            phases: int = 0, out: Optional[torch.Tensor] = None, check: bool = False,
+            validate: bool = True, wait_cycles: int = 0, flags: int = 0, split_tiles: int = 0,
+            use_error_word: bool = True):
     """Delta-attention prefill of one layer.
 
     q [b, H, s, d], k/v [b, Hkv, s, d] (post-RoPE; any strides with d
     contiguous).  Returns ``out`` [b, s, H, d] in q's dtype (computation in
     bf16, as the reference's sparse path does, ``delta_attention/llama.py:383-388``),
     and, with ``return_anchor_delta``, the fp32 anchor deltas [b, n_anchor, H, d].
+    An explicit ``anchors`` list is checked on the host (``validate``; it
+    must start at 0, increase strictly and stay below ``s_p``).  ``check``
+    synchronises and raises if a kernel recorded an error (see
+    :func:`check_errors`); ``wait_cycles``, ``flags`` and ``split_tiles`` are
+    the C ABI's (0 = defaults).  With ``use_error_word=False`` kernel codes go
+    to the workspace header instead (read with :func:`check_workspace`).
     """
     _check_cuda(q, k, v)
     odt = q.dtype
@@ -92,8 +162,13 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
     a.gamma, a.window, a.sink, a.q_block = int(gamma), int(window), int(sink), int(q_block)
     a.mode = _lib.MODES[mode]
     a.phases = int(phases)
+    a.split_tiles = int(split_tiles)
     anc = None
     if anchors is not None:
+        if s_p is None:
+            raise ValueError("explicit anchors need s_p")
+        if validate:
+            _validate_anchors(anchors, int(s_p), s)
         anc = anchors.to(device=q.device, dtype=torch.int32).contiguous()
         a.anchors = _ptr(anc)
         a.n_anchors = anc.numel()
@@ -101,11 +176,14 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
     ws_bytes = lib().dta_prefill_workspace_size(ctypes.byref(a))
     if ws_bytes == 0:
         # let dta_prefill report the precise validation status
-        check(lib().dta_prefill(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_prefill")
+        _check_status(lib().dta_prefill(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_prefill")
     if workspace is None or workspace.numel() < ws_bytes:
         workspace = _workspace(ws_bytes, q.device)
     a.workspace = _ptr(workspace)
     a.workspace_bytes = workspace.numel()
+    a.error_word = _ptr(error_word(q.device)) if use_error_word else None
+    a.wait_cycles = int(wait_cycles)
+    a.flags = int(flags)
     delta = None
     if return_anchor_delta and mode == "delta":
         if anc is not None:
@@ -115,21 +193,25 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
             n_anchor = max(s - cut_n, 0) // gamma
         delta = torch.empty(b, n_anchor, H, d, dtype=torch.float32, device=q.device)
         a.anchor_delta = _ptr(delta)
-    check(lib().dta_prefill(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_prefill")
+    _check_status(lib().dta_prefill(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_prefill")
+    if check:
+        check_errors(q.device)
     if odt != torch.bfloat16:
         out = out.to(odt)
     return (out, delta) if return_anchor_delta else out
 
 
 def prefill_workspace(batch: int, n_heads: int, n_kv_heads: int, seq_len: int, head_dim: int, *, gamma: int,
-                      mode: str = "delta", n_anchors: Optional[int] = None, s_p: Optional[int] = None,
-                      device=None) -> torch.Tensor:
+                      window: int = 0, sink: int = 0, mode: str = "delta", n_anchors: Optional[int] = None,
+                      s_p: Optional[int] = None, split_tiles: int = 0, device=None) -> torch.Tensor:
     """A device workspace of the size ``dta_prefill_workspace_size`` reports, for
-    callers that keep one workspace across calls."""
+    callers that keep one workspace across calls (on the current device; pass
+    the window and sink of the calls it will serve)."""
     a = PrefillArgs()
     a.abi_version = ABI_VERSION
     a.batch, a.n_heads, a.n_kv_heads, a.seq_len, a.head_dim = batch, n_heads, n_kv_heads, seq_len, head_dim
-    a.gamma, a.window, a.sink, a.q_block, a.mode = int(gamma), 0, 0, 64, _lib.MODES[mode]
+    a.gamma, a.window, a.sink, a.q_block, a.mode = int(gamma), int(window), int(sink), 64, _lib.MODES[mode]
+    a.split_tiles = int(split_tiles)
     if n_anchors is not None:
         a.anchors, a.n_anchors, a.s_p = 16, int(n_anchors), int(s_p)
     nbytes = lib().dta_prefill_workspace_size(ctypes.byref(a))
@@ -139,7 +221,8 @@ def prefill_workspace(batch: int, n_heads: int, n_kv_heads: int, seq_len: int, h
 
 
 def anchor_deltas(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rows: torch.Tensor, *, window: int,
-                  sink: int, scaling: Optional[float] = None, q_block: int = 64) -> torch.Tensor:
+                  sink: int, scaling: Optional[float] = None, q_block: int = 64,
+                  validate: bool = True) -> torch.Tensor:
     """dense - sparse (fp32) at the given sorted query rows, [b, n, H, d].
 
     Runs only the row launch of the prefill (dense and sparse attention of the
@@ -150,15 +233,17 @@ def anchor_deltas(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rows: torch
     dummy = torch.empty(16, dtype=torch.bfloat16, device=q.device)
     _, delta = prefill(q, k, v, gamma=1, window=window, sink=sink, scaling=scaling, mode="delta",
                        q_block=q_block, anchors=rows, s_p=s, return_anchor_delta=True,
-                       phases=_lib.PHASE_ROWS, out=dummy)
+                       phases=_lib.PHASE_ROWS, out=dummy, validate=validate)
     return delta
 
 
 def rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_rows: torch.Tensor, kv_limit: torch.Tensor,
-         scaling: Optional[float] = None) -> torch.Tensor:
+         scaling: Optional[float] = None, *, check: bool = False, validate: bool = True,
+         wait_cycles: int = 0, flags: int = 0, split_tiles: int = 0) -> torch.Tensor:
     """Attention for a list of query rows: row i uses ``q[:, :, q_rows[i]]`` and
     attends keys ``[0, kv_limit[i]]`` (non-decreasing).  Returns [b, n, H, d]
-    (the ``qsa_kernel`` contract, ``delta_attention/delta_kernel.py:259-329``)."""
+    (the ``qsa_kernel`` contract, ``delta_attention/delta_kernel.py:259-329``).
+    The lists are checked on the host unless ``validate`` is False."""
     _check_cuda(q, k, v)
     odt = q.dtype
     qb, kb, vb = _bf16_lastdim_contig(q), _bf16_lastdim_contig(k), _bf16_lastdim_contig(v)
@@ -166,6 +251,8 @@ def rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_rows: torch.Tensor
     Hkv, skv = kb.shape[1], kb.shape[2]
     if scaling is None:
         scaling = d ** -0.5
+    if validate:
+        _validate_rows(q_rows, kv_limit, sq, skv)
     qr = q_rows.to(device=q.device, dtype=torch.int32).contiguous()
     kl = kv_limit.to(device=q.device, dtype=torch.int32).contiguous()
     n = qr.numel()
@@ -183,9 +270,18 @@ def rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_rows: torch.Tensor
     a.q_rows, a.kv_limit = _ptr(qr), _ptr(kl)
     a.out = _ptr(out)
     a.scaling = float(scaling)
-    ws = _workspace(lib().dta_rows_workspace_size(ctypes.byref(a)), q.device)
+    a.error_word = _ptr(error_word(q.device))
+    a.wait_cycles = int(wait_cycles)
+    a.flags = int(flags)
+    a.split_tiles = int(split_tiles)
+    ws_bytes = lib().dta_rows_workspace_size(ctypes.byref(a))
+    if ws_bytes == 0:
+        _check_status(lib().dta_rows(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_rows")
+    ws = _workspace(ws_bytes, q.device)
     a.workspace, a.workspace_bytes = _ptr(ws), ws.numel()
-    check(lib().dta_rows(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_rows")
+    _check_status(lib().dta_rows(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_rows")
+    if check:
+        check_errors(q.device)
     return out if odt == torch.bfloat16 else out.to(odt)
 
 
@@ -219,7 +315,7 @@ def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, window: int, si
     a.dense_out, a.sparse_out = _ptr(dense), _ptr(sparse)
     ws = _workspace(lib().dta_decode_workspace_size(ctypes.byref(a)), q.device)
     a.workspace, a.workspace_bytes = _ptr(ws), ws.numel()
-    check(lib().dta_decode(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_decode")
+    _check_status(lib().dta_decode(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_decode")
     return dense, sparse
 
 
@@ -228,5 +324,5 @@ def check_workspace(workspace: torch.Tensor) -> int:
     code = ctypes.c_int(0)
     st = lib().dta_check_workspace(ctypes.c_void_p(_ptr(workspace)), ctypes.c_void_p(_stream()),
                                    ctypes.byref(code))
-    check(st, f"kernel error word {code.value}")
+    _check_status(st, f"kernel error word {code.value}")
     return code.value

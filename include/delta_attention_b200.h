@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define DTA_ABI_VERSION 1
+#define DTA_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define DTA_API __attribute__((visibility("default")))
@@ -50,7 +50,8 @@ typedef enum dta_status {
   DTA_ERR_WORKSPACE = 7,        /* workspace missing or smaller than *_workspace_size */
   DTA_ERR_CUDA = 8,             /* a CUDA runtime call failed (see dta_last_cuda_error) */
   DTA_ERR_UNSUPPORTED_DEVICE = 9, /* current device is not sm_100 */
-  DTA_ERR_KERNEL_TIMEOUT = 10,  /* a kernel gave up on a bounded wait (dta_check_workspace) */
+  DTA_ERR_KERNEL_TIMEOUT = 10,  /* a kernel gave up on a bounded wait or met an out-of-range row
+                                   (dta_check_workspace / the caller's error_word) */
   DTA_ERR_SCRATCH_LIMIT = 11    /* dta_decode_noalloc: request needs more scratch than its static array */
 } dta_status;
 
@@ -94,7 +95,25 @@ typedef struct dta_prefill_args {
   int32_t phases;         /* 0 = whole prefill; otherwise a mask of DTA_PHASE_* */
   void* workspace;
   size_t workspace_bytes;
+  int32_t* error_word;    /* optional device int32: kernels record a timeout or bad-row code
+                             here (atomically, first code wins) instead of in the workspace
+                             header; never cleared by the library, so it stays set across
+                             calls until the caller reads and clears it */
+  int64_t wait_cycles;    /* budget of each bounded wait inside the kernels, in SM clock
+                             cycles; 0 = the default (~2 s) */
+  int32_t flags;          /* mask of DTA_FLAG_* (0 for normal use) */
+  int32_t split_tiles;    /* key tiles (128 keys) per split-K chunk of the dense rows; 0 = chosen
+                             from the device's SM count and the total work.  A dense row tile
+                             longer than this runs as several chunks whose partial results the
+                             last-finishing chunk merges (log-sum-exp); see dta_prefill_workspace_size */
 } dta_prefill_args;
+
+/* Test hook: the producer warp of every CTA first waits on a barrier that
+ * nothing ever completes, so that wait runs out after wait_cycles, the CTA
+ * abandons its work and the launch records a kernel timeout code.  Lets a
+ * test check the timeout path without any faulting or hanging input.
+ * Outputs of such a call are not written. */
+#define DTA_FLAG_TEST_STALL 1
 
 /* Phases of dta_prefill.  ROWS: dense rows (anchors + tail) and sparse anchor
  * rows, written to the workspace (and anchor_delta when given).  WINDOW: the
@@ -131,6 +150,10 @@ typedef struct dta_rows_args {
   float scaling;
   void* workspace;
   size_t workspace_bytes;
+  int32_t* error_word;    /* as in dta_prefill_args */
+  int64_t wait_cycles;    /* as in dta_prefill_args */
+  int32_t flags;          /* as in dta_prefill_args */
+  int32_t split_tiles;    /* as in dta_prefill_args */
 } dta_rows_args;
 DTA_API size_t dta_rows_workspace_size(const dta_rows_args* args);
 DTA_API int dta_rows(const dta_rows_args* args, void* stream);

@@ -62,18 +62,84 @@ def test_validation_status(override, status):
     assert L.dta_prefill(ctypes.byref(a), None) == status
 
 
+def _split_bytes(BG, n_sel, JR, d, sms, tiles_of, factor=3, min_tiles=16):
+    """Restates the library's split-K sizing of the rows launch (dta_api.cu
+    plan_rows_split): chunks of at most total/(sms*factor) key tiles."""
+    ndt = (n_sel + JR - 1) // JR
+    T = [tiles_of(t) for t in range(ndt)]
+    total = sum(T) * BG
+    chunk = max(min_tiles, -(-total // (sms * factor)))
+    cmax = -(-max(T) // chunk)
+    if cmax <= 1:
+        return 0, 1
+    al = lambda x: (x + 255) // 256 * 256
+    slots = BG * ndt * cmax * 2 * 128
+    return al(BG * ndt * 2 * 4 * 4) + al(slots * d * 4) + al(slots * 4), cmax
+
+
 def test_workspace_size_query():
+    """No GPU here: the library sizes for a B200's 148 SMs."""
     L = _lib.lib()
-    a = _prefill_args(seq_len=131072)
-    n_anchor = (131072 - 128) // 64
-    expect = 256 + 2 * ((1 * n_anchor * 32 * 128 * 4 + 255) // 256 * 256) \
-        + (1 * n_anchor * 32 * 128 * 2 + 255) // 256 * 256  # fp32 dense + sparse, bf16 delta
+    s, gamma = 131072, 64
+    a = _prefill_args(seq_len=s)
+    n_anchor = (s - 128) // gamma
+    s_p = n_anchor * gamma
+    n_sel = n_anchor + 128
+
+    def tiles_of(t):
+        i = min((t + 1) * 64, n_sel) - 1
+        pos = i * gamma if i < n_anchor else s_p + (i - n_anchor)
+        return pos // 128 + 1
+
+    split, cmax = _split_bytes(8, n_sel, 64, 128, 148, tiles_of)
+    assert cmax > 1  # config 2: the dense tail (1024 key tiles) is split
+    expect = 256 + split + 2 * ((1 * n_anchor * 32 * 128 * 4 + 255) // 256 * 256) \
+        + (1 * n_anchor * 32 * 128 * 2 + 255) // 256 * 256  # counters+partials, fp32 dense + sparse, bf16 delta
     assert L.dta_prefill_workspace_size(ctypes.byref(a)) == expect
     a.mode = 2  # sparse-only needs only the header
     assert L.dta_prefill_workspace_size(ctypes.byref(a)) == 256
     a.workspace = None
     a.mode = 0
     assert L.dta_prefill(ctypes.byref(a), None) == 7
+
+
+def test_v2_fields_validated():
+    L = _lib.lib()
+    a = _prefill_args()
+    a.workspace, a.workspace_bytes = 1 << 20, 1 << 30
+    a.flags = 4  # unknown flag
+    assert L.dta_prefill(ctypes.byref(a), None) == 1
+    a.flags, a.wait_cycles = 0, -5
+    assert L.dta_prefill(ctypes.byref(a), None) == 1
+    a.wait_cycles, a.error_word = 0, (1 << 20) + 2  # not 4-byte aligned
+    assert L.dta_prefill(ctypes.byref(a), None) == 4
+    a.error_word, a.split_tiles = None, -1
+    assert L.dta_prefill(ctypes.byref(a), None) == 1
+
+
+def test_status_strings_cover_every_status():
+    L = _lib.lib()
+    for st in _lib.STATUS_NAMES:
+        assert L.dta_status_string(st).decode() != "unknown status", st
+
+
+def test_host_validation_of_lists():
+    import torch
+    from delta_attention_b200 import ops
+    with pytest.raises(ValueError, match="anchors"):
+        ops._validate_anchors(torch.tensor([0, 64, 64]), 256, 384)
+    with pytest.raises(ValueError, match="anchors"):
+        ops._validate_anchors(torch.tensor([1, 64]), 256, 384)
+    with pytest.raises(ValueError, match="anchors"):
+        ops._validate_anchors(torch.tensor([0, 300]), 256, 384)
+    ops._validate_anchors(torch.tensor([0, 5, 255]), 256, 384)
+    with pytest.raises(ValueError, match="q_rows"):
+        ops._validate_rows(torch.tensor([0, 600]), torch.tensor([0, 1]), 512, 512)
+    with pytest.raises(ValueError, match="kv_limit"):
+        ops._validate_rows(torch.tensor([0, 1]), torch.tensor([0, 512]), 512, 512)
+    with pytest.raises(ValueError, match="non-decreasing"):
+        ops._validate_rows(torch.tensor([0, 1]), torch.tensor([5, 4]), 512, 512)
+    ops._validate_rows(torch.tensor([0, 1]), torch.tensor([4, 5]), 512, 512)
 
 
 def test_ops_refuse_cpu_tensors():

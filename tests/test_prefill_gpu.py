@@ -178,3 +178,39 @@ def test_error_status_raises():
     q, k, v = make_inputs(1000, 4, 1, 128, seed=1, device="cuda")
     with pytest.raises(DtaError, match="GAMMA"):
         ops.prefill(q, k, v, gamma=48, window=128, sink=16)
+
+
+@pytest.mark.parametrize("s,H,Hkv,d,gamma,window,sink,split", [
+    (2048, 8, 2, 128, 64, 256, 64, 1),     # fused delta, every dense row tile split per key tile
+    (2048, 8, 1, 128, 16, 384, 32, 3),     # GQA 8, gamma 16 (sparse anchor jobs + delta kernel)
+    (1536, 16, 2, 128, 128, 256, 128, 2),  # GQA 8, gamma 128
+    (2000, 4, 1, 128, 8, 300, 50, 5),      # ragged length: partial last row tile
+    (1280, 8, 2, 64, 32, 256, 64, 2),      # head_dim 64
+])
+def test_split_dense_rows_match_oracle(s, H, Hkv, d, gamma, window, sink, split):
+    """Split-K of the dense rows forced at small sizes: each row tile's keys run
+    as several chunks whose partials the last chunk merges.  The result must
+    match the oracle and the unsplit kernel (split_tiles larger than any row)."""
+    q, k, v = make_inputs(s, H, Hkv, d, seed=40 + split + gamma)
+    out, delta = _run(q, k, v, gamma=gamma, window=window, sink=sink, split_tiles=split,
+                      return_anchor_delta=True)
+    whole, delta_whole = _run(q, k, v, gamma=gamma, window=window, sink=sink, split_tiles=1 << 20,
+                              return_anchor_delta=True)
+    torch.cuda.synchronize()
+    from delta_attention_b200 import ops
+    ops.check_errors()
+    ref = _oracle_full(q, k, v, gamma, window, sink)
+    assert_close(out.cpu(), ref, f"split {split}: s={s} H={H}/{Hkv} d={d} g={gamma}")
+    assert_close(out.cpu(), whole.cpu(), f"split {split} vs unsplit")
+    assert_close(delta.cpu(), delta_whole.cpu(), f"split {split} anchor delta vs unsplit")
+
+
+def test_rows_op_split_matches_dense_rows():
+    """dta_rows with one key tile per chunk: long rows merge up to 12 partials."""
+    s, H, Hkv, d = 1536, 8, 2, 128
+    q, k, v = make_inputs(s, H, Hkv, d, seed=15)
+    rows = torch.tensor([0, 5, 127, 128, 300, 777, 1000, 1200, 1400, 1535])
+    from delta_attention_b200 import ops
+    out = ops.rows(q.cuda(), k.cuda(), v.cuda(), rows, rows, split_tiles=1, check=True)
+    ref = orc.dense_rows(q.float(), k.float(), v.float(), rows, d ** -0.5)
+    assert_close(out.cpu(), ref, "rows op, split per key tile")
