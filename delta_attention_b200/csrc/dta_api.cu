@@ -14,6 +14,7 @@
 #include "dta_decode.h"
 #include "dta_internal.h"
 #include "dta_prefill.h"
+#include "dta_ptx.cuh"
 
 namespace {
 thread_local int g_last_cuda_error = 0;
@@ -113,6 +114,7 @@ inline bool stride_ok(long long s) { return s > 0 && (s * 2) % 16 == 0; }
 #endif
 constexpr int kSplitFactor = DTA_SPLIT_FACTOR;
 constexpr int kSplitMinTiles = DTA_SPLIT_MIN_TILES;
+constexpr int kMaxChunks = 16384;  // chunks per row tile (the kernel packs the count in 15 bits)
 
 struct RowsSplit {
   int n_dense_tiles = 0;
@@ -136,11 +138,15 @@ RowsSplit plan_rows_split(int BG, int n_sel, int JR, int head_dim, int sms, long
     if (T > t_max) t_max = T;
   }
   const long long c0 = (total + (long long)sms * kSplitFactor - 1) / ((long long)sms * kSplitFactor);
-  const int chunk = forced > 0 ? forced : (int)(c0 < kSplitMinTiles ? kSplitMinTiles : c0);
+  // no split when the longest row tile is within 10% of the work per SM: the
+  // longest-first order of whole tiles is then balanced already
+  if (forced <= 0 && (long long)t_max * 10 <= total * 11 / sms) return S;
+  int chunk = forced > 0 ? forced : (int)(c0 < kSplitMinTiles ? kSplitMinTiles : c0);
+  if ((t_max + chunk - 1) / chunk > kMaxChunks) chunk = (t_max + kMaxChunks - 1) / kMaxChunks;
   const int cmax = (t_max + chunk - 1) / chunk;
   if (cmax <= 1) return S;
   S.cmax = cmax;
-  S.c = (t_max + cmax - 1) / cmax;
+  S.c = chunk;
   const size_t slots = (size_t)BG * S.n_dense_tiles * cmax * dta::PREFILL_NQ * 128;
   S.part_o_bytes = align_up(slots * head_dim * 4, 256);
   S.part_lse_bytes = align_up(slots * 4, 256);
@@ -305,7 +311,7 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   p.seq_q = S;
   p.kv_len = S;
   p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
-  p.wait_cycles = a->wait_cycles;
+  p.wait_cycles = a->wait_cycles > 0 ? a->wait_cycles : dta::kWaitTimeoutCycles;
   p.test_stall = (a->flags & DTA_FLAG_TEST_STALL) ? 1 : 0;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
   p.counter = reinterpret_cast<int*>(ws);
@@ -339,6 +345,7 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
     if (e != cudaSuccess) return fail_cuda(e);
   }
   const bool fuse = L.fuse;
+  bool rows_launched = false;
   // launch 1: dense rows (anchors + tail) and, unless fused, sparse anchor rows
   if ((phases & DTA_PHASE_ROWS) && a->mode != DTA_MODE_SPARSE_ONLY && L.n_sel > 0) {
     dta::PrefillParams r = p;
@@ -350,7 +357,8 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
     r.split_cmax = L.split.cmax;
     r.n_jobs = (r.n_dense_tiles * L.split.cmax + r.n_sparse_tiles) * B * Hkv;
     const int grid = r.n_jobs < sms ? r.n_jobs : sms;
-    if ((e = dta::launch_prefill(r, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
+    if ((e = dta::launch_prefill(r, d, grid, false, stream)) != cudaSuccess) return fail_cuda(e);
+    rows_launched = true;
   }
   // delta = dense - sparse per anchor (bf16 for the windowed launch, fp32 telemetry on request)
   if ((phases & DTA_PHASE_ROWS) && L.buf_bytes && !fuse) {
@@ -374,7 +382,9 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
     w.n_jobs = w.n_window_tiles * B * Hkv;
     if (w.n_jobs > 0) {
       const int grid = w.n_jobs < sms ? w.n_jobs : sms;
-      if ((e = dta::launch_prefill(w, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
+      // queued right behind this call's rows launch (or its delta kernel): its
+      // CTAs may start on SMs the rows launch no longer needs
+      if ((e = dta::launch_prefill(w, d, grid, rows_launched, stream)) != cudaSuccess) return fail_cuda(e);
     }
   }
   // (runs between the two launches, stream-ordered)
@@ -461,7 +471,7 @@ int dta_rows(const dta_rows_args* a, void* stream_) {
   p.seq_q = a->seq_len;
   p.kv_len = a->kv_len;
   p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
-  p.wait_cycles = a->wait_cycles;
+  p.wait_cycles = a->wait_cycles > 0 ? a->wait_cycles : dta::kWaitTimeoutCycles;
   p.test_stall = (a->flags & DTA_FLAG_TEST_STALL) ? 1 : 0;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
   p.counter = reinterpret_cast<int*>(ws);
@@ -485,7 +495,7 @@ int dta_rows(const dta_rows_args* a, void* stream_) {
   cudaError_t e = cudaMemsetAsync(a->workspace, 0, kHeaderBytes + S.cnt_bytes, stream);
   if (e != cudaSuccess) return fail_cuda(e);
   const int grid = p.n_jobs < sms ? p.n_jobs : sms;
-  if ((e = dta::launch_prefill(p, d, grid, stream)) != cudaSuccess) return fail_cuda(e);
+  if ((e = dta::launch_prefill(p, d, grid, false, stream)) != cudaSuccess) return fail_cuda(e);
   return DTA_OK;
 }
 

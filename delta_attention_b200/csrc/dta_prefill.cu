@@ -145,6 +145,10 @@ struct Ctrl {
   Plan plan[2];             // key-tile plan of job[slot], computed once by the producer
   uint32_t tmem_base;
   int abort_flag;
+  // split dense jobs: per softmax warp, (chunk | active chunks << 16) of its
+  // current job, or -1; kept here so it is not held in registers across the
+  // key-tile loop
+  int split_word[4 * NQ];
 };
 static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block too large");
 static_assert(offsetof(Ctrl, dslot) % 16 == 0, "dslot is read with 16-byte loads");
@@ -157,9 +161,13 @@ __device__ __forceinline__ uint32_t bits_from(int lo) {
   return lo <= 0 ? 0xffffffffu : (lo >= 32 ? 0u : (0xffffffffu << lo));
 }
 
-template <int HD>
+// LK (a Launch) is a compile-time parameter: the windowed kernel carries no
+// row-list, split-K or dense-row code and the rows kernel no staging, TMA-store
+// or fused-delta code, so each role is register-allocated for its own launch.
+template <int HD, int LK>
 __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
   using G = Geo<HD>;
+  constexpr bool WIN = (LK == LAUNCH_WINDOW);
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
@@ -175,7 +183,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   const int lane = threadIdx.x & 31;
   volatile int* abort_flag = &ctrl->abort_flag;
   int* err = p.error;
-  const WaitCtx wc{abort_flag, err, p.wait_cycles > 0 ? p.wait_cycles : kWaitTimeoutCycles};
+  // (the budget is read from the launch parameters, not held in a register)
+  const WaitCtx wc{abort_flag, err, p.wait_cycles};
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -212,11 +221,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     ctrl->abort_flag = 0;
     mbar_init_fence();
   }
+  // rows launch: a windowed launch queued behind this one may start its CTAs
+  // as this grid's CTAs run out of jobs and exit
+  if (!WIN && threadIdx.x == 0) grid_dependents_launch();
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
-    if (p.launch == LAUNCH_WINDOW) tma_prefetch_desc(&p.tm_q);
-    if (p.tma_out) tma_prefetch_desc(&p.tm_out);
+    if (WIN) tma_prefetch_desc(&p.tm_q);
+    if (WIN && p.tma_out) tma_prefetch_desc(&p.tm_out);
   }
   // Every warp must be converged at a CTA barrier (bar.sync counts whole
   // warps) and at the warp-collective TMEM alloc/dealloc.
@@ -253,7 +265,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       Plan P{};
       for (;;) {
         int j;
-        if (p.launch == LAUNCH_WINDOW) {
+        if constexpr (WIN) {
           j = blockIdx.x + (fetched++) * gridDim.x;
         } else {
           int jj = 0;
@@ -286,7 +298,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         if (!mbar_wait_warp(BAR(q_empty[0]) + 8 * qs, (q_fills[qs] & 1) ^ 1, wc, KERR_TIMEOUT_PRODUCER))
           return false;
         ++q_fills[qs];
-        if (J.kind == JOB_WINDOW) {
+        if constexpr (WIN) {
           if (lane == 0) {
             mbar_arrive_expect_tx(BAR(q_full[0]) + 8 * qs, G::TILE_BYTES);
             for (int r = 0; r < G::REGIONS; ++r)
@@ -525,6 +537,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     int jobs_done = 0;  // jobs in which this query tile was active
     int st_rounds = 0;  // 64-column TMA-store rounds through this tile's staging half
     bool st_pending = false;  // (leader) the last round's store has not been waited for
+    bool dep_done = false;  // the rows launch's output may be read (windowed launch)
     int f_writes = 0;   // fused delta: anchor rows published by tile A so far
     int f_reads = 0;    // fused delta: of those, read by tile B
     for (int it = 0;; ++it) {
@@ -537,19 +550,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       }
       const Plan P = ctrl->plan[slot];  // read before the slot is released
       __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(job_empty[0]) + 8 * slot);
+      if (lane == 0) {
+        mbar_arrive(BAR(job_empty[0]) + 8 * slot);
+        ctrl->split_word[warp - 4] =
+            (!WIN && J.kind == JOB_DENSE_ROWS && P.n_chunks > 1) ? (P.chunk | ((q ? P.act_t[1] : P.act_t[0]) << 16))
+                                                                 : -1;
+      }
       if (J.kind == JOB_END) break;
       // this warpgroup's tile: selects, not a dynamic index, so the plan stays in registers
       const int T = q ? P.tiles_t[1] : P.tiles_t[0];
       // Window-launch tiles whose 128 rows all lie below row_end leave through
       // this tile's staging half and TMA stores (recompute mode skips anchor
       // rows, so it stores row by row).
-      const bool use_stg = p.tma_out && J.kind == JOB_WINDOW && p.mode != 1 && T > 0 &&
+      const bool use_stg = WIN && p.tma_out && p.mode != 1 && T > 0 &&
                            J.start + (q + 1) * p.R <= p.row_end;
       // fused delta (windowed launch, gamma 64, 4 heads per group): tile A's
       // row 0 of each head is the job's anchor; tile A publishes dense - sparse
       // for it and tile B reads it.  Both warpgroups count every job.
-      const bool fuse = p.fuse_delta && J.kind == JOB_WINDOW;
+      const bool fuse = WIN && p.fuse_delta;
       const int f_writes_prev = f_writes, f_reads_prev = f_reads;
       if (fuse && P.tiles_t[0] > 0) ++f_writes;
       if (fuse && P.tiles_t[0] > 0 && P.tiles_t[1] > 0) ++f_reads;
@@ -557,7 +575,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       const int li = q * p.R + rr;  // job-local row
       const bool row_valid = li < J.count;
       const int qpos = row_valid ? job_row_pos(p, J, li) : (q ? P.qmax_t[1] : P.qmax_t[0]);
-      const bool sparse_kind = (J.kind != JOB_DENSE_ROWS);
+      const bool sparse_kind = WIN || (J.kind != JOB_DENSE_ROWS);
       const int lo_q = sparse_kind ? block_window_lo(p, qpos) : 0;
       const int sink_q = sparse_kind ? p.sink : 0x7fffffff;
       const int qmin_t = q ? P.qmin_t[1] : P.qmin_t[0];
@@ -565,14 +583,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       // L1 now for the epilogue at the end of the job
       const __nv_bfloat16* dlt = nullptr;
       const long long anchor_row = ((long long)J.b * p.n_anchor + anchor_of(p, qpos)) * p.H + J.g * p.G + hh;
+      // (prefetches of the rows launch's output only once it has completed:
+      // before that, under a programmatic dependent launch, it may be unwritten)
       if (fuse) {
         // tile A: its head's anchor dense row (fp32, written by the rows launch)
         // goes to L2 now; each lane loads 4 columns of it at the end of the job
-        if (q == 0 && lane < HD * 4 / 128)
+        if (q == 0 && lane < HD * 4 / 128 && dep_done)
           asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(p.dense_buf + anchor_row * HD) + lane * 128));
-      } else if (J.kind == JOB_WINDOW && p.mode == 0 && p.delta_buf) {
+      } else if (WIN && p.mode == 0 && p.delta_buf) {
         dlt = p.delta_buf + anchor_row * HD;
-        asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char*>(dlt) + (lane & (HD * 2 / 128 - 1)) * 128));
+        if (dep_done)
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char*>(dlt) + (lane & (HD * 2 / 128 - 1)) * 128));
       }
       const int lo_max_t = q ? P.lo_max_t[1] : P.lo_max_t[0];
 
@@ -723,7 +744,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       bool store = row_valid;
       int mode_out = 0;  // 0: bf16 to out, 1: fp32 to dense_buf, 2: fp32 to sparse_buf
       long long out_row = 0;
-      if (J.kind == JOB_WINDOW) {
+      if constexpr (WIN) {
         out_row = qpos;
         if (store && p.mode == 1) {
           store = !is_anchor_row(p, qpos);
@@ -745,6 +766,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       const float inv_l = (l_run > 0.f) ? __fdividef(1.f, l_run) : 0.f;
       // (fused delta, tile A: this lane's 4 columns of the anchor's dense row,
       // loaded while the last PV runs)
+      if (WIN && !dep_done) {
+        // the rows launch (the grid this one may overlap) has completed and its
+        // writes are visible before the first read of its output
+        grid_dependency_wait();
+        dep_done = true;
+      }
       const float4 dn4 = (fuse && q == 0)
                              ? __ldg(reinterpret_cast<const float4*>(p.dense_buf + anchor_row * HD) + (lane & (HD / 4 - 1)))
                              : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -760,22 +787,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(o_empty[0]) + 8 * q);
       ++jobs_done;
-      if (J.kind == JOB_DENSE_ROWS && P.n_chunks > 1) {
+      if constexpr (!WIN) {
+      __syncwarp();
+      const int split_word = *reinterpret_cast<volatile int*>(&ctrl->split_word[warp - 4]);
+      if (split_word >= 0) {
         // ---- split dense job: store this chunk's partial (O / l and the
         // log2-sum-exp of every row); the chunk that finishes last merges all
         // of them and stores the rows ----
         const int r_shift = __ffs(p.R) - 1;
         const long long tile_id = (long long)(J.b * p.Hkv + J.g) * p.n_dense_tiles + (J.start >> (r_shift + 1));
-        const int act = q ? P.act_t[1] : P.act_t[0];
+        const int act = split_word >> 16;
+        const int chunk = split_word & 0xffff;
         auto slot_of = [&](int k) { return ((tile_id * p.split_cmax + k) * NQ + q) * 128; };
         const float lse = (l_run > 0.f) ? m_run + __log2f(l_run) : -INFINITY;
         {
-          float4* po = reinterpret_cast<float4*>(p.part_o) + slot_of(P.chunk) * (HD / 4) + r;
+          float4* po = reinterpret_cast<float4*>(p.part_o) + slot_of(chunk) * (HD / 4) + r;
 #pragma unroll
           for (int c4 = 0; c4 < HD / 4; ++c4)
             po[c4 * 128] = make_float4(o[4 * c4] * inv_l, o[4 * c4 + 1] * inv_l, o[4 * c4 + 2] * inv_l,
                                        o[4 * c4 + 3] * inv_l);
-          p.part_lse[slot_of(P.chunk) + r] = lse;
+          p.part_lse[slot_of(chunk) + r] = lse;
         }
         // Each warp counts its own 32 rows' chunks (no barrier across the
         // warpgroup, whose warps may leave the job loop independently on an
@@ -791,12 +822,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         // Last chunk: log-sum-exp merge of the tile's active chunks, read back
         // from L2 (bypassing L1) 32 columns at a time, so this thread's own O
         // is no longer needed in registers; the rows are stored from here.
-        float M = -INFINITY;
-        for (int k = 0; k < act; ++k) M = fmaxf(M, __ldcg(p.part_lse + slot_of(k) + r));
-        float wsum = 0.f;
-        for (int k = 0; k < act; ++k) {
-          const float lk = __ldcg(p.part_lse + slot_of(k) + r);
-          wsum += (lk == -INFINITY) ? 0.f : fast_exp2(lk - M);
+        // max and weight sum in one online pass, four loads in flight
+        float M = -INFINITY, wsum = 0.f;
+        for (int k0 = 0; k0 < act; k0 += 4) {
+          float l4[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) l4[u] = (k0 + u < act) ? __ldcg(p.part_lse + slot_of(k0 + u) + r) : -INFINITY;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (l4[u] == -INFINITY) continue;
+            if (l4[u] > M) {
+              wsum = (M == -INFINITY) ? 1.f : fmaf(wsum, fast_exp2(M - l4[u]), 1.f);
+              M = l4[u];
+            } else {
+              wsum += fast_exp2(l4[u] - M);
+            }
+          }
         }
         const float inv_w = (wsum > 0.f) ? __fdividef(1.f, wsum) : 0.f;
         __nv_bfloat16* dbf = (store && mode_out == 0)
@@ -804,24 +845,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
                                  : nullptr;
         float* dfl = (store && mode_out == 1) ? p.dense_buf + (((long long)J.b * p.n_anchor + gli) * p.H + h) * HD
                                               : nullptr;
+        // weighted sum, 32 columns at a time, four chunks' loads in flight
 #pragma unroll 1
         for (int cb = 0; cb < HD / 32; ++cb) {
           float acc[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) acc[e] = 0.f;
-          for (int k = 0; k < act; ++k) {
-            const float lk = __ldcg(p.part_lse + slot_of(k) + r);
-            const float w = (lk == -INFINITY) ? 0.f : fast_exp2(lk - M) * inv_w;
-            const float4* pk = reinterpret_cast<const float4*>(p.part_o) + slot_of(k) * (HD / 4) + cb * 8 * 128 + r;
-            float4 v4[8];
+          for (int k0 = 0; k0 < act; k0 += 4) {
+            float w4[4];
+            float4 v4[4][8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) v4[u] = __ldcg(pk + u * 128);
+            for (int u = 0; u < 4; ++u) {
+              const int k = (k0 + u < act) ? k0 + u : k0;  // past the end: reload chunk k0, weight 0
+              w4[u] = __ldcg(p.part_lse + slot_of(k) + r);
+              const float4* pk = reinterpret_cast<const float4*>(p.part_o) + slot_of(k) * (HD / 4) + cb * 8 * 128 + r;
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              acc[4 * u] = fmaf(w, v4[u].x, acc[4 * u]);
-              acc[4 * u + 1] = fmaf(w, v4[u].y, acc[4 * u + 1]);
-              acc[4 * u + 2] = fmaf(w, v4[u].z, acc[4 * u + 2]);
-              acc[4 * u + 3] = fmaf(w, v4[u].w, acc[4 * u + 3]);
+              for (int e = 0; e < 8; ++e) v4[u][e] = __ldcg(pk + e * 128);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float w = (k0 + u >= act || w4[u] == -INFINITY) ? 0.f : fast_exp2(w4[u] - M) * inv_w;
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                acc[4 * e] = fmaf(w, v4[u][e].x, acc[4 * e]);
+                acc[4 * e + 1] = fmaf(w, v4[u][e].y, acc[4 * e + 1]);
+                acc[4 * e + 2] = fmaf(w, v4[u][e].z, acc[4 * e + 2]);
+                acc[4 * e + 3] = fmaf(w, v4[u][e].w, acc[4 * e + 3]);
+              }
             }
           }
           if (dfl) {
@@ -841,6 +891,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         }
         continue;
       }
+      }  // !WIN
       const uint64_t inv2 = f2_pack(inv_l, inv_l);
       __nv_bfloat16* dst_bf = (store && mode_out == 0)
                                   ? p.out + (((long long)J.b * p.out_rows + out_row) * p.H + h) * HD
@@ -988,6 +1039,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
 #undef BAR
   // bulk (TMA) stores of this thread complete before the CTA exits
   if (warp >= 4 && (warp & 3) == 0 && lane == 0) bulk_wait_all();
+  // a windowed CTA never completes before the grid it depends on (also when
+  // it read none of that grid's output)
+  if (WIN && threadIdx.x == 0) grid_dependency_wait();
   __syncwarp();
   tc_fence_before();
   __syncthreads();
@@ -998,18 +1052,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   }
 }
 
-template <int HD>
-static cudaError_t launch_prefill_hd(const PrefillParams& p, int grid, cudaStream_t stream) {
+template <int HD, int LK>
+static cudaError_t launch_prefill_hd(const PrefillParams& p, int grid, bool dependent, cudaStream_t stream) {
   const int smem = Geo<HD>::SMEM_BYTES;
-  cudaError_t e = cudaFuncSetAttribute(prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaFuncSetAttribute(prefill_kernel<HD, LK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  prefill_kernel<HD><<<grid, NUM_THREADS, smem, stream>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = dependent ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, prefill_kernel<HD, LK>, p);
 }
 
-cudaError_t launch_prefill(const PrefillParams& p, int head_dim, int grid, cudaStream_t stream) {
-  if (head_dim == 128) return launch_prefill_hd<128>(p, grid, stream);
-  return launch_prefill_hd<64>(p, grid, stream);
+cudaError_t launch_prefill(const PrefillParams& p, int head_dim, int grid, bool dependent, cudaStream_t stream) {
+  const bool win = p.launch == LAUNCH_WINDOW;
+  if (head_dim == 128)
+    return win ? launch_prefill_hd<128, LAUNCH_WINDOW>(p, grid, dependent, stream)
+               : launch_prefill_hd<128, LAUNCH_ROWS>(p, grid, false, stream);
+  return win ? launch_prefill_hd<64, LAUNCH_WINDOW>(p, grid, dependent, stream)
+             : launch_prefill_hd<64, LAUNCH_ROWS>(p, grid, false, stream);
 }
 
 }  // namespace dta

@@ -56,8 +56,8 @@ struct PrefillParams {
   __nv_bfloat16* out;           // [B, out_rows, H, d]
   int tma_out;                  // window launch: full tiles leave through tm_out (TMA stores)
   // Split-K of the rows launch's dense jobs.  A dense job (one row tile of the
-  // list) whose key range spans T tiles runs as c = min(ceil(T / split_c),
-  // split_cmax) jobs ("chunks") over equal key ranges; each chunk stores its
+  // list) whose key range spans T > split_c tiles runs as c = ceil(T / split_c)
+  // jobs ("chunks") over key tiles [k split_c, (k+1) split_c); each chunk stores its
   // rows' O / l and log2-sum-exp as partials, and the chunk that finishes last
   // (per query tile and warp, counted in part_cnt) merges them and stores the
   // rows.  split_c == 0: no split (one chunk per row tile).  The job index
@@ -67,7 +67,7 @@ struct PrefillParams {
   float* part_o;                // [B*Hkv][n_dense_tiles][split_cmax][NQ][d/4][128] float4
   float* part_lse;              // [B*Hkv][n_dense_tiles][split_cmax][NQ][128]
   int* part_cnt;                // [B*Hkv][n_dense_tiles][NQ][4 warps] chunks finished, zeroed by the host
-  long long wait_cycles;        // budget of each bounded wait (clock64 cycles)
+  long long wait_cycles;        // budget of each bounded wait (clock64 cycles, > 0)
   int test_stall;               // test hook: the producer first waits on a barrier nothing completes
   int seq_q, kv_len;            // rows of q and of k/v: bounds for explicit row lists
 };
@@ -86,7 +86,10 @@ __device__ __forceinline__ int fast_div(int n, unsigned long long mul, int sh) {
   return (int)(((unsigned long long)(unsigned)n * mul) >> sh);
 }
 
-cudaError_t launch_prefill(const PrefillParams& p, int head_dim, int grid, cudaStream_t stream);
+// `dependent`: the windowed launch may start while the rows launch queued just
+// before it on the stream is still running (programmatic dependent launch); it
+// waits for that grid before reading its output.
+cudaError_t launch_prefill(const PrefillParams& p, int head_dim, int grid, bool dependent, cudaStream_t stream);
 // delta = dense - sparse per anchor: bf16 into delta_bf16 (for the windowed
 // launch) and, when delta_f32 is not null, fp32 into delta_f32 (telemetry).
 cudaError_t launch_anchor_delta(const float* dense, const float* sparse, __nv_bfloat16* delta_bf16, float* delta_f32,

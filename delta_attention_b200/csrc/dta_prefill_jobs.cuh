@@ -37,8 +37,8 @@ __device__ __forceinline__ int list_kv_limit(const PrefillParams& p, int i) {
 
 // Job index -> job.  Window launch: (batch x group)-major R*NQ-row tiles of
 // rows [0, row_end).  Rows launch: dense row tiles longest first (each with
-// split_cmax chunk slots), then sparse anchor tiles; the batch x group index
-// varies fastest.
+// split_cmax chunk slots), then sparse anchor tiles; without split-K the
+// batch x group index varies fastest, with it the order is group-major.
 static __device__ Job decode_job(const PrefillParams& p, int j) {
   Job J;
   const int JR = PREFILL_NQ * p.R;  // rows per job
@@ -59,10 +59,23 @@ static __device__ Job decode_job(const PrefillParams& p, int j) {
     return J;
   }
   const int BG = p.B * p.Hkv;
-  const int u = j / BG, bg = j - (j / BG) * BG;
+  const int cmax = p.split_cmax > 0 ? p.split_cmax : 1;
+  int u, bg;
+  if (cmax > 1) {
+    // split: group-major (all CTAs sweep one group's K/V together, so each
+    // key chunk is read from DRAM about once); the chunks are short enough
+    // that the longest-first order inside each group keeps the SMs balanced
+    const int per_bg = p.n_dense_tiles * cmax + p.n_sparse_tiles;
+    bg = j / per_bg;
+    u = j - bg * per_bg;
+  } else {
+    // whole row tiles: longest first across groups (the longest tiles bound
+    // the launch and must start first)
+    u = j / BG;
+    bg = j - u * BG;
+  }
   J.b = bg / p.Hkv;
   J.g = bg - J.b * p.Hkv;
-  const int cmax = p.split_cmax > 0 ? p.split_cmax : 1;
   if (u < p.n_dense_tiles * cmax) {
     const int rank = u / cmax;
     const int tile = p.n_dense_tiles - 1 - rank;  // longest (latest rows) first
@@ -145,13 +158,16 @@ static __device__ Plan make_plan(const PrefillParams& p, const Job& J) {
     P.qmax = max(P.qmax, P.qmax_t[q]);
   }
   if (dense) {
-    // key tiles [kb, ke) of this chunk out of the row tile's T
+    // key tiles [kb, ke) of this chunk out of the row tile's T.  Chunk
+    // boundaries are multiples of split_c for every row tile, so chunk k of
+    // all row tiles (running at about the same time, longest-first order)
+    // read the same key range of their group and share it in L2.
     const int T = P.qmax / PREFILL_BN + 1;
     int c = 1, kb = 0, ke = T;
-    if (p.split_c > 0) {
+    if (p.split_c > 0 && T > p.split_c) {
       c = min((T + p.split_c - 1) / p.split_c, p.split_cmax);
-      kb = (int)((long long)J.chunk * T / c);
-      ke = (int)((long long)(J.chunk + 1) * T / c);
+      kb = J.chunk * p.split_c;
+      ke = (J.chunk == c - 1) ? T : kb + p.split_c;
     }
     P.n_chunks = c;
     P.n0 = 0;
@@ -175,8 +191,8 @@ static __device__ Plan make_plan(const PrefillParams& p, const Job& J) {
       }
       const int Tq = m / PREFILL_BN + 1;
       P.tiles_t[q] = min(max(Tq - kb, 0), ke - kb);
-      // chunk k' has keys for tile q iff floor(k' T / c) < Tq, i.e. k' < Tq c / T
-      P.act_t[q] = min(c, (int)(((long long)Tq * c + T - 1) / T));
+      // chunk k' has keys for tile q iff it starts below Tq: k' split_c < Tq
+      P.act_t[q] = (c == 1) ? 1 : min(c, (Tq + p.split_c - 1) / p.split_c);
     }
     return P;
   }

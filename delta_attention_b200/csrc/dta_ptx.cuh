@@ -131,6 +131,13 @@ __device__ __forceinline__ bool mbar_poll(uint32_t bar, uint32_t parity, const W
   return mbar_poll_slow(bar, parity, w, code);
 }
 
+// Programmatic dependent launch: the dependent grid's wait for the grid it
+// depends on (complete, writes visible), and the primary's early trigger.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Warp-collective variant: every lane waits, then the warp reconverges so the
 // caller may issue .sync.aligned tcgen05 instructions.  The result is the
 // AND over the warp (an abort seen by any lane aborts the whole warp).

@@ -228,12 +228,17 @@ def anchor_deltas(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rows: torch
     Runs only the row launch of the prefill (dense and sparse attention of the
     listed rows); used by the adaptive stride planner."""
     s = q.shape[2]
+    if validate:
+        r = rows.detach().to("cpu", torch.int64)
+        if r.numel() == 0 or int(r.min()) < 0 or int(r.max()) >= s or \
+                (r.numel() > 1 and not bool((r[1:] > r[:-1]).all())):
+            raise ValueError(f"rows must be strictly increasing and lie in [0, {s})")
     rows = rows.to(device=q.device, dtype=torch.int32)
     # no tail rows (s_p == s) and no windowed launch: `out` is never written
     dummy = torch.empty(16, dtype=torch.bfloat16, device=q.device)
     _, delta = prefill(q, k, v, gamma=1, window=window, sink=sink, scaling=scaling, mode="delta",
                        q_block=q_block, anchors=rows, s_p=s, return_anchor_delta=True,
-                       phases=_lib.PHASE_ROWS, out=dummy, validate=validate)
+                       phases=_lib.PHASE_ROWS, out=dummy, validate=False)
     return delta
 
 

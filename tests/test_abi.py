@@ -64,10 +64,13 @@ def test_validation_status(override, status):
 
 def _split_bytes(BG, n_sel, JR, d, sms, tiles_of, factor=3, min_tiles=16):
     """Restates the library's split-K sizing of the rows launch (dta_api.cu
-    plan_rows_split): chunks of at most total/(sms*factor) key tiles."""
+    plan_rows_split): no split while the longest row tile is within 10% of the
+    work per SM, else chunks of at most total/(sms*factor) key tiles."""
     ndt = (n_sel + JR - 1) // JR
     T = [tiles_of(t) for t in range(ndt)]
     total = sum(T) * BG
+    if max(T) * 10 <= total * 11 // sms:
+        return 0, 1
     chunk = max(min_tiles, -(-total // (sms * factor)))
     cmax = -(-max(T) // chunk)
     if cmax <= 1:
@@ -77,11 +80,14 @@ def _split_bytes(BG, n_sel, JR, d, sms, tiles_of, factor=3, min_tiles=16):
     return al(BG * ndt * 2 * 4 * 4) + al(slots * d * 4) + al(slots * 4), cmax
 
 
-def test_workspace_size_query():
-    """No GPU here: the library sizes for a B200's 148 SMs."""
+@pytest.mark.parametrize("heads,kv_heads,split_expected", [(32, 8, False), (4, 1, True)])
+def test_workspace_size_query(heads, kv_heads, split_expected):
+    """No GPU here: the library sizes for a B200's 148 SMs.  Config 2 on one GPU
+    (8 KV groups) is balanced without split-K; one KV group (the per-GPU share
+    at 8-GPU strong scaling) splits the long dense row tiles."""
     L = _lib.lib()
     s, gamma = 131072, 64
-    a = _prefill_args(seq_len=s)
+    a = _prefill_args(seq_len=s, n_heads=heads, n_kv_heads=kv_heads)
     n_anchor = (s - 128) // gamma
     s_p = n_anchor * gamma
     n_sel = n_anchor + 128
@@ -91,10 +97,10 @@ def test_workspace_size_query():
         pos = i * gamma if i < n_anchor else s_p + (i - n_anchor)
         return pos // 128 + 1
 
-    split, cmax = _split_bytes(8, n_sel, 64, 128, 148, tiles_of)
-    assert cmax > 1  # config 2: the dense tail (1024 key tiles) is split
-    expect = 256 + split + 2 * ((1 * n_anchor * 32 * 128 * 4 + 255) // 256 * 256) \
-        + (1 * n_anchor * 32 * 128 * 2 + 255) // 256 * 256  # counters+partials, fp32 dense + sparse, bf16 delta
+    split, cmax = _split_bytes(kv_heads, n_sel, 64, 128, 148, tiles_of)
+    assert (cmax > 1) == split_expected
+    expect = 256 + split + 2 * ((1 * n_anchor * heads * 128 * 4 + 255) // 256 * 256) \
+        + (1 * n_anchor * heads * 128 * 2 + 255) // 256 * 256  # counters+partials, fp32 dense + sparse, bf16 delta
     assert L.dta_prefill_workspace_size(ctypes.byref(a)) == expect
     a.mode = 2  # sparse-only needs only the header
     assert L.dta_prefill_workspace_size(ctypes.byref(a)) == 256
