@@ -546,8 +546,10 @@ def run_b200(args, rank, world, local_rank):
             "cpu_baseline": cpu,
             "e2e": e2e,
             # two prefill launches per step, plus the delta kernel unless the
-            # windowed launch forms delta itself (gamma 64, 4 heads per KV head)
-            "gpu_launches": (2 if (args.gamma == 64 and G == 4) else 3) * args.steps,
+            # windowed launch forms delta itself (4 or 8 heads per KV head,
+            # gamma a power of two >= 8)
+            "gpu_launches": (2 if (G in (4, 8) and args.gamma >= 8 and args.gamma & (args.gamma - 1) == 0)
+                             else 3) * args.steps,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -169,6 +169,8 @@ int sizing_sms() {
 struct PrefillLayout {
   int s_p, n_anchor, n_sel;
   bool fuse;           // the windowed launch forms delta itself (no sparse anchor jobs)
+  bool delta_cross;    // ... in the first job of each anchor period, for the period's other tiles
+  int win_group;       // windowed jobs per anchor period when it spans several, else 1
   int n_sparse_tiles;  // sparse anchor row tiles of the rows launch
   RowsSplit split;
   size_t buf_bytes;    // one of dense_buf / sparse_buf (fp32)
@@ -205,13 +207,16 @@ int prefill_layout(const dta_prefill_args* a, int sms, PrefillLayout* L) {
     L->n_anchor = s_p / a->gamma;
     L->n_sel = L->n_anchor + cut_n;
   }
-  // With gamma = 64, uniform anchors and 4 heads per KV group, every 64-row job
-  // of the windowed launch starts at its anchor row, so that launch forms
-  // delta = dense - sparse itself from the anchor row's own sparse output and
-  // the rows launch skips the sparse anchor rows (and the delta kernel).  Both
-  // phases derive the choice from the arguments alone.
-  L->fuse = a->mode == DTA_MODE_DELTA && !a->anchors && a->gamma == 64 && G == 4 && L->n_anchor > 0;
+  // With uniform anchors, 4 or 8 heads per KV group and gamma a power of two
+  // >= 8, the windowed launch forms delta = dense - sparse itself from each
+  // anchor row's own sparse output, and the rows launch skips the sparse anchor
+  // rows (and the delta kernel).  Both phases derive the choice from the
+  // arguments alone.
   const int R = 128 / G, JR = dta::PREFILL_NQ * R, BG = a->batch * a->n_kv_heads;
+  const bool pow2 = a->gamma >= 8 && (a->gamma & (a->gamma - 1)) == 0;
+  L->fuse = a->mode == DTA_MODE_DELTA && !a->anchors && L->n_anchor > 0 && (G == 4 || G == 8) && pow2;
+  L->delta_cross = L->fuse && a->gamma > R;
+  L->win_group = (L->fuse && a->gamma > JR) ? a->gamma / JR : 1;
   L->n_sparse_tiles = (a->mode == DTA_MODE_DELTA && !L->fuse) ? (L->n_anchor + JR - 1) / JR : 0;
   if (L->n_sel > 0) {
     // a sparse anchor tile spans its rows' window plus the rows' own spread
@@ -372,6 +377,9 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
     dta::PrefillParams w = p;
     w.launch = dta::LAUNCH_WINDOW;
     w.fuse_delta = fuse;
+    w.delta_cross = L.delta_cross;
+    w.win_group = L.win_group;
+    w.delta_pair = fuse && G == 4 && a->gamma == 2 * R;
     w.anchor_delta_f32 = fuse ? a->anchor_delta : nullptr;
     // out [B, S, H, d] seen as (d, s, H, B) with a (64, R, G, 1) box: one box is
     // one query tile, rows in the tile's order (head-major), so full tiles
@@ -381,7 +389,8 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
     w.n_window_tiles = (w.row_end + JR - 1) / JR;
     w.n_jobs = w.n_window_tiles * B * Hkv;
     if (w.n_jobs > 0) {
-      const int grid = w.n_jobs < sms ? w.n_jobs : sms;
+      const int groups = w.n_jobs / w.win_group;  // (win_group divides the tiles of every group)
+      const int grid = groups < sms ? groups : sms;
       // queued right behind this call's rows launch (or its delta kernel): its
       // CTAs may start on SMs the rows launch no longer needs
       if ((e = dta::launch_prefill(w, d, grid, rows_launched, stream)) != cudaSuccess) return fail_cuda(e);

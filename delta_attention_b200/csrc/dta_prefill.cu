@@ -136,22 +136,25 @@ struct Ctrl {
   uint64_t s_full[NQ], p_full[NQ * 2], o_full[NQ], o_empty[NQ];
   uint64_t stg_full[NQ];    // tile q's rows are in its staging half (4 warps)
   uint64_t stg_free[NQ];    // the last TMA store from tile q's staging half has read it
-  uint64_t delta_ready;     // fused delta: tile A wrote this job's anchor rows (4 warps)
-  uint64_t delta_free;      // fused delta: tile B read them (4 warps)
   uint64_t drain;
   uint64_t stall;           // test hook: a barrier that nothing completes
-  alignas(16) uint32_t dslot[4][64];  // fused delta: bf16 (dense - sparse) row of each head's anchor (read as uint4)
+  uint64_t delta_ready;     // pair delta: tile A wrote this job's anchor rows (4 warps)
+  uint64_t delta_free;      // pair delta: tile B read them (4 warps)
+  alignas(16) uint32_t dslot[4][64];  // pair delta: bf16 (dense - sparse) row of each head's anchor (read as uint4)
   int job[2][8];
   Plan plan[2];             // key-tile plan of job[slot], computed once by the producer
   uint32_t tmem_base;
   int abort_flag;
+  // fused delta across warps: anchor rows formed so far by this CTA's warps
+  // (one count per forming warp and anchor period; only ever grows)
+  int delta_count;
   // split dense jobs: per softmax warp, (chunk | active chunks << 16) of its
   // current job, or -1; kept here so it is not held in registers across the
   // key-tile loop
   int split_word[4 * NQ];
 };
-static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block too large");
 static_assert(offsetof(Ctrl, dslot) % 16 == 0, "dslot is read with 16-byte loads");
+static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block too large");
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -161,13 +164,17 @@ __device__ __forceinline__ uint32_t bits_from(int lo) {
   return lo <= 0 ? 0xffffffffu : (lo >= 32 ? 0u : (0xffffffffu << lo));
 }
 
-// LK (a Launch) is a compile-time parameter: the windowed kernel carries no
-// row-list, split-K or dense-row code and the rows kernel no staging, TMA-store
-// or fused-delta code, so each role is register-allocated for its own launch.
-template <int HD, int LK>
+// LK (a Launch) and FM (a FuseMode, windowed launch) are compile-time
+// parameters: the windowed kernel carries no row-list, split-K or dense-row
+// code and the rows kernel no staging, TMA-store or fused-delta code, and each
+// fused-delta arrangement has its own windowed kernel, so every variant is
+// register-allocated for its own work.
+template <int HD, int LK, int FM>
 __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
   using G = Geo<HD>;
   constexpr bool WIN = (LK == LAUNCH_WINDOW);
+  constexpr bool FUSE = WIN && FM != FUSE_NONE;  // the windowed launch forms the delta
+  constexpr bool PAIR = WIN && FM == FUSE_PAIR;  // ... tile A for tile B through shared memory
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
@@ -214,11 +221,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       mbar_init(BAR(stg_full[0]) + 8 * q, 4);
       mbar_init(BAR(stg_free[0]) + 8 * q, 1);
     }
-    mbar_init(BAR(delta_ready), 4);
-    mbar_init(BAR(delta_free), 4);
     mbar_init(BAR(drain), 1);
     mbar_init(BAR(stall), 1);
+    mbar_init(BAR(delta_ready), 4);
+    mbar_init(BAR(delta_free), 4);
     ctrl->abort_flag = 0;
+    ctrl->delta_count = 0;
     mbar_init_fence();
   }
   // rows launch: a windowed launch queued behind this one may start its CTAs
@@ -266,7 +274,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       for (;;) {
         int j;
         if constexpr (WIN) {
-          j = blockIdx.x + (fetched++) * gridDim.x;
+          // static stride over groups of win_group consecutive jobs (one
+          // anchor period when it spans several jobs, so the job forming its
+          // delta runs first, on this CTA)
+          const int f = fetched++;
+          j = (FM != FUSE_GENERAL || p.win_group == 1)
+                  ? blockIdx.x + f * gridDim.x
+                  : (blockIdx.x + (f / p.win_group) * gridDim.x) * p.win_group + f % p.win_group;
         } else {
           int jj = 0;
           if (lane == 0) jj = atomicAdd(p.counter, 1);
@@ -538,8 +552,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
     int st_rounds = 0;  // 64-column TMA-store rounds through this tile's staging half
     bool st_pending = false;  // (leader) the last round's store has not been waited for
     bool dep_done = false;  // the rows launch's output may be read (windowed launch)
-    int f_writes = 0;   // fused delta: anchor rows published by tile A so far
-    int f_reads = 0;    // fused delta: of those, read by tile B
+    int periods = 0;    // fused delta across warps: anchor periods this tile has entered
+    int f_writes = 0;   // pair delta: anchor rows published by tile A so far
+    int f_reads = 0;    // pair delta: of those, read by tile B
     for (int it = 0;; ++it) {
       const int slot = it & 1;
       if (!mbar_wait_warp(BAR(job_full[0]) + 8 * slot, (it >> 1) & 1, wc, KERR_TIMEOUT_SOFTMAX)) break;
@@ -564,13 +579,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       // rows, so it stores row by row).
       const bool use_stg = WIN && p.tma_out && p.mode != 1 && T > 0 &&
                            J.start + (q + 1) * p.R <= p.row_end;
-      // fused delta (windowed launch, gamma 64, 4 heads per group): tile A's
-      // row 0 of each head is the job's anchor; tile A publishes dense - sparse
-      // for it and tile B reads it.  Both warpgroups count every job.
-      const bool fuse = WIN && p.fuse_delta;
+      // fused delta (windowed launch, uniform anchors): the warp holding an
+      // anchor row forms dense - sparse for it in its epilogue; with anchors
+      // at most R apart every warp forms its own rows' anchors, otherwise the
+      // first job of each anchor period forms them in tile A and the other
+      // tiles of the period wait for them (delta_count)
+      constexpr bool fuse = FUSE;
+      // pair delta (gamma = 64 with 4 heads per group: a 64-row job starts at
+      // its anchor, which is row 0 of tile A for every head): tile A hands each
+      // head's delta row to tile B through shared memory.  Both warpgroups
+      // count every job.
+      constexpr bool pair = PAIR;
       const int f_writes_prev = f_writes, f_reads_prev = f_reads;
-      if (fuse && P.tiles_t[0] > 0) ++f_writes;
-      if (fuse && P.tiles_t[0] > 0 && P.tiles_t[1] > 0) ++f_reads;
+      if (pair && P.tiles_t[0] > 0) ++f_writes;
+      if (pair && P.tiles_t[0] > 0 && P.tiles_t[1] > 0) ++f_reads;
+      if (fuse && !pair && p.delta_cross && J.start == fast_div(J.start, p.gamma_mul, p.gamma_sh) * p.gamma)
+        ++periods;
       if (T == 0) continue;  // this query tile is empty in this job
       const int li = q * p.R + rr;  // job-local row
       const bool row_valid = li < J.count;
@@ -585,11 +609,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       const long long anchor_row = ((long long)J.b * p.n_anchor + anchor_of(p, qpos)) * p.H + J.g * p.G + hh;
       // (prefetches of the rows launch's output only once it has completed:
       // before that, under a programmatic dependent launch, it may be unwritten)
-      if (fuse) {
+      if (pair) {
         // tile A: its head's anchor dense row (fp32, written by the rows launch)
         // goes to L2 now; each lane loads 4 columns of it at the end of the job
         if (q == 0 && lane < HD * 4 / 128 && dep_done)
           asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(p.dense_buf + anchor_row * HD) + lane * 128));
+      } else if (fuse) {
+        // an anchor row's dense row (fp32, written by the rows launch) goes to
+        // L2 now; the warp reads it at the end of the job to form the delta
+        // (anchor rows: recomputed in the epilogue rather than held across the key loop)
+        if (row_valid && qpos == fast_div(qpos, p.gamma_mul, p.gamma_sh) * p.gamma && dep_done) {
+#pragma unroll
+          for (int c = 0; c < HD * 4 / 128; ++c)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(p.dense_buf + anchor_row * HD) + c * 128));
+        }
       } else if (WIN && p.mode == 0 && p.delta_buf) {
         dlt = p.delta_buf + anchor_row * HD;
         if (dep_done)
@@ -764,17 +797,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       }
       // 1/l to ~2 ulp (__fdividef): far below the bf16 rounding of the output
       const float inv_l = (l_run > 0.f) ? __fdividef(1.f, l_run) : 0.f;
-      // (fused delta, tile A: this lane's 4 columns of the anchor's dense row,
-      // loaded while the last PV runs)
       if (WIN && !dep_done) {
         // the rows launch (the grid this one may overlap) has completed and its
-        // writes are visible before the first read of its output
+        // writes are visible before the first read of its output.  Its output
+        // (the dense rows) is read through L2 only (ld.global.cg): this grid
+        // started while that one ran, so neither the non-coherent read-only
+        // path nor L1 is guaranteed to hold current copies of it.
         grid_dependency_wait();
         dep_done = true;
       }
-      const float4 dn4 = (fuse && q == 0)
-                             ? __ldg(reinterpret_cast<const float4*>(p.dense_buf + anchor_row * HD) + (lane & (HD / 4 - 1)))
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      // fused delta: the anchor rows among this warp's rows, and this lane's 4
+      // columns of the dense row of the warp's first anchor (loaded while the
+      // last PV runs)
+      uint32_t anchor_mask = 0;
+      float4 dn_first = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (pair) {
+        // tile A: lane 0 of every warp holds its head's anchor row
+        if (q == 0) dn_first = __ldcg(reinterpret_cast<const float4*>(p.dense_buf + anchor_row * HD) + (lane & (HD / 4 - 1)));
+      } else if (fuse) {
+        anchor_mask = __ballot_sync(0xffffffffu, row_valid && qpos == fast_div(qpos, p.gamma_mul, p.gamma_sh) * p.gamma);
+        if (anchor_mask) {
+          const long long arow0 = __shfl_sync(0xffffffffu, anchor_row, __ffs(anchor_mask) - 1);
+          dn_first = __ldcg(reinterpret_cast<const float4*>(p.dense_buf + arow0 * HD) + (lane & (HD / 4 - 1)));
+        } else if (p.delta_cross) {
+          // a consumer tile: its rows' delta lines into L1 early (a prefetch is
+          // only a hint; the read after the delta_count wait is what is ordered)
+#pragma unroll
+          for (int c = 0; c < HD * 2 / 128; ++c)
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char*>(p.delta_buf + anchor_row * HD) + c * 128));
+        }
+      }
       // o_full[q] completes once per job of this tile (after its last PV); the
       // next job's first PV waits for o_empty[q], so phases cannot run ahead
       if (!mbar_wait_warp(BAR(o_full[0]) + 8 * q, jobs_done & 1, wc, KERR_TIMEOUT_SOFTMAX)) break;
@@ -913,9 +965,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
             !mbar_wait_warp(BAR(stg_free[0]) + 8 * q, (st_rounds - 1) & 1, wc, KERR_TIMEOUT_SOFTMAX))
           break;
       }
-      // the anchor's bf16 delta row: global (dlt) or, fused, this head's slot
+      // the anchor's bf16 delta row: written by the delta kernel (dlt) or,
+      // fused, formed here by the warp that holds the anchor row
       const uint4* dsrc = reinterpret_cast<const uint4*>(dlt);
-      if (fuse) {
+      if (pair) {
         if (q == 0) {
           // the slot is free once tile B has read the previous job's rows
           if (f_reads_prev > 0 &&
@@ -923,8 +976,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
             break;
           // lane 0's row is the anchor (position J.start).  Its raw O row goes
           // through the first 512 bytes of this warp's own staging rows; each
-          // lane scales its 4 columns by the anchor's 1/l (sparse = O / l, exactly
-          // as the rows launch would store it) and forms dense - sparse
+          // lane scales its 4 columns by the anchor's 1/l and forms dense - sparse
           float4* tmp = reinterpret_cast<float4*>(base + G::STG_OFF + quarter * 32 * 128);  // tile A's half
           if (lane == 0) {
 #pragma unroll
@@ -935,8 +987,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           if (lane < HD / 4) {
             const float inv_l0 = reinterpret_cast<const float*>(tmp)[HD];
             const float4 ot = tmp[lane];
-            const float4 sp = make_float4(ot.x * inv_l0, ot.y * inv_l0, ot.z * inv_l0, ot.w * inv_l0);
-            const float4 d = make_float4(dn4.x - sp.x, dn4.y - sp.y, dn4.z - sp.z, dn4.w - sp.w);
+            const float4 d = make_float4(dn_first.x - ot.x * inv_l0, dn_first.y - ot.y * inv_l0,
+                                         dn_first.z - ot.z * inv_l0, dn_first.w - ot.w * inv_l0);
             ctrl->dslot[quarter][2 * lane] = pack_bf16x2(d.x, d.y);
             ctrl->dslot[quarter][2 * lane + 1] = pack_bf16x2(d.z, d.w);
             if (p.anchor_delta_f32) reinterpret_cast<float4*>(p.anchor_delta_f32 + anchor_row * HD)[lane] = d;
@@ -947,7 +999,59 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           break;
         }
         dsrc = reinterpret_cast<const uint4*>(&ctrl->dslot[quarter][0]);
+      } else if (fuse) {
+        // each anchor row of this warp: its raw O row and 1/l go through this
+        // warp's own staging rows; each lane forms 4 columns of
+        // dense - O / l (the sparse row exactly as the rows launch would store
+        // it) and writes them to the anchor's delta slot
+        float4* tmp = reinterpret_cast<float4*>(base + G::STG_OFF + q * G::STG_HALF + quarter * 32 * 128);
+        uint32_t mask = anchor_mask;
+        bool first = true;
+        while (mask) {
+          const int al = __ffs(mask) - 1;
+          mask &= mask - 1;
+          if (lane == al) {
+#pragma unroll
+            for (int c4 = 0; c4 < HD / 4; ++c4) tmp[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
+            reinterpret_cast<float*>(tmp)[HD] = inv_l;
+          }
+          __syncwarp();
+          const long long arow = __shfl_sync(0xffffffffu, anchor_row, al);
+          if (lane < HD / 4) {
+            const float inv_l0 = reinterpret_cast<const float*>(tmp)[HD];
+            const float4 ot = tmp[lane];
+            const float4 dn = first ? dn_first : __ldcg(reinterpret_cast<const float4*>(p.dense_buf + arow * HD) + lane);
+            const float4 d = make_float4(dn.x - ot.x * inv_l0, dn.y - ot.y * inv_l0, dn.z - ot.z * inv_l0,
+                                         dn.w - ot.w * inv_l0);
+            reinterpret_cast<uint2*>(p.delta_buf + arow * HD)[lane] = make_uint2(pack_bf16x2(d.x, d.y), pack_bf16x2(d.z, d.w));
+            if (p.anchor_delta_f32) reinterpret_cast<float4*>(p.anchor_delta_f32 + arow * HD)[lane] = d;
+          }
+          __syncwarp();  // the staging rows may be reused
+          first = false;
+        }
+        if (p.delta_cross) {
+          if (anchor_mask) {
+            // publish: this warp's delta rows are visible to the CTA
+            __threadfence_block();
+            __syncwarp();
+            if (lane == 0) atomicAdd(&ctrl->delta_count, 1);
+          } else {
+            // the four warps of this period's forming tile have published
+            if (!__all_sync(0xffffffffu, smem_wait_geq(&ctrl->delta_count, 4 * periods, wc, KERR_TIMEOUT_SOFTMAX)))
+              break;
+            __threadfence_block();
+          }
+        }
+        dsrc = reinterpret_cast<const uint4*>(p.delta_buf + anchor_row * HD);
+        // rows formed by this warp just now: into L1 ahead of the stores (the
+        // rows are written and read by this SM only, in this launch)
+        if (anchor_mask) {
+#pragma unroll
+          for (int c = 0; c < HD * 2 / 128; ++c)
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char*>(dsrc) + c * 128));
+        }
       }
+      auto dload = [&](int i) -> uint4 { return dsrc ? dsrc[i] : make_uint4(0, 0, 0, 0); };
       if (use_stg) {
         // row r of the tile (head r / R, position r % R: the order of the
         // (64, R, G, 1) box) as a 128-byte-swizzled 128-byte row of this tile's
@@ -963,7 +1067,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
 #pragma unroll
           for (int cw = 0; cw < 8; ++cw) {
             const int c16 = rg * 8 + cw;
-            const uint4 dv = dsrc ? dsrc[c16] : make_uint4(0, 0, 0, 0);
+            const uint4 dv = dload(c16);
             const uint32_t dw4[4] = {dv.x, dv.y, dv.z, dv.w};
             uint32_t w[4];
 #pragma unroll
@@ -1007,7 +1111,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           uint32_t ww[16];
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
-            const uint4 w = dsrc ? dsrc[c * 4 + v4] : make_uint4(0, 0, 0, 0);
+            const uint4 w = dload(c * 4 + v4);
             ww[4 * v4] = w.x; ww[4 * v4 + 1] = w.y; ww[4 * v4 + 2] = w.z; ww[4 * v4 + 3] = w.w;
           }
 #pragma unroll
@@ -1030,7 +1134,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           *reinterpret_cast<float4*>(dst_f + e) =
               make_float4(o[e] * inv_l, o[e + 1] * inv_l, o[e + 2] * inv_l, o[e + 3] * inv_l);
       }
-      if (fuse && q == 1) {
+      if (pair && q == 1) {
         __syncwarp();  // every lane has read the slot
         if (lane == 0) mbar_arrive(BAR(delta_free));
       }
@@ -1052,10 +1156,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
   }
 }
 
-template <int HD, int LK>
+template <int HD, int LK, int FM>
 static cudaError_t launch_prefill_hd(const PrefillParams& p, int grid, bool dependent, cudaStream_t stream) {
   const int smem = Geo<HD>::SMEM_BYTES;
-  cudaError_t e = cudaFuncSetAttribute(prefill_kernel<HD, LK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaFuncSetAttribute(prefill_kernel<HD, LK, FM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -1067,16 +1171,22 @@ static cudaError_t launch_prefill_hd(const PrefillParams& p, int grid, bool depe
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = dependent ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, prefill_kernel<HD, LK>, p);
+  return cudaLaunchKernelEx(&cfg, prefill_kernel<HD, LK, FM>, p);
 }
 
 cudaError_t launch_prefill(const PrefillParams& p, int head_dim, int grid, bool dependent, cudaStream_t stream) {
-  const bool win = p.launch == LAUNCH_WINDOW;
-  if (head_dim == 128)
-    return win ? launch_prefill_hd<128, LAUNCH_WINDOW>(p, grid, dependent, stream)
-               : launch_prefill_hd<128, LAUNCH_ROWS>(p, grid, false, stream);
-  return win ? launch_prefill_hd<64, LAUNCH_WINDOW>(p, grid, dependent, stream)
-             : launch_prefill_hd<64, LAUNCH_ROWS>(p, grid, false, stream);
+  const int fm = !p.fuse_delta ? FUSE_NONE : (p.delta_pair ? FUSE_PAIR : FUSE_GENERAL);
+  if (p.launch != LAUNCH_WINDOW)
+    return head_dim == 128 ? launch_prefill_hd<128, LAUNCH_ROWS, FUSE_NONE>(p, grid, false, stream)
+                           : launch_prefill_hd<64, LAUNCH_ROWS, FUSE_NONE>(p, grid, false, stream);
+  if (head_dim == 128) {
+    if (fm == FUSE_PAIR) return launch_prefill_hd<128, LAUNCH_WINDOW, FUSE_PAIR>(p, grid, dependent, stream);
+    if (fm == FUSE_GENERAL) return launch_prefill_hd<128, LAUNCH_WINDOW, FUSE_GENERAL>(p, grid, dependent, stream);
+    return launch_prefill_hd<128, LAUNCH_WINDOW, FUSE_NONE>(p, grid, dependent, stream);
+  }
+  if (fm == FUSE_PAIR) return launch_prefill_hd<64, LAUNCH_WINDOW, FUSE_PAIR>(p, grid, dependent, stream);
+  if (fm == FUSE_GENERAL) return launch_prefill_hd<64, LAUNCH_WINDOW, FUSE_GENERAL>(p, grid, dependent, stream);
+  return launch_prefill_hd<64, LAUNCH_WINDOW, FUSE_NONE>(p, grid, dependent, stream);
 }
 
 }  // namespace dta

@@ -9,6 +9,10 @@
 namespace dta {
 
 enum Launch : int { LAUNCH_ROWS = 0, LAUNCH_WINDOW = 1 };
+// How the windowed launch obtains each anchor's delta (PrefillParams fields
+// fuse_delta / delta_pair): from the delta kernel, handed from tile A to tile B
+// through shared memory, or formed by the warp holding the anchor row.
+enum FuseMode : int { FUSE_NONE = 0, FUSE_PAIR = 1, FUSE_GENERAL = 2 };
 
 // Query tiles (of 128 rows = R rows x G heads) per kernel job: the two tiles
 // of a job ping-pong on the tensor core (dta_prefill.cu).
@@ -46,12 +50,18 @@ struct PrefillParams {
   int* error;                   // kernel error word, zeroed by the host
   float* dense_buf;             // [B, n_anchor, H, d] fp32
   float* sparse_buf;            // [B, n_anchor, H, d] fp32
-  const __nv_bfloat16* delta_buf;  // [B, n_anchor, H, d] bf16: dense - sparse (window launch)
-  // window launch: form delta = dense - sparse inside the kernel from each job's
-  // own anchor row (gamma == 64 with 4 heads per KV group: a 64-row job starts at
-  // its anchor, which is row 0 of tile A for every head); the rows launch then
-  // computes no sparse anchor rows
-  int fuse_delta;
+  __nv_bfloat16* delta_buf;     // [B, n_anchor, H, d] bf16: dense - sparse (window launch)
+  // window launch: form delta = dense - sparse inside the kernel from each
+  // anchor row's own sparse output (uniform anchors, 4 or 8 heads per KV
+  // group, gamma a power of two >= 8); the rows launch then computes no sparse
+  // anchor rows and no delta kernel runs.  delta_cross: anchors are more than
+  // R rows apart, so the first job of each anchor period forms them (tile A)
+  // for the other tiles of the period; win_group: jobs per anchor period when
+  // it spans several (processed consecutively by one CTA), else 1.
+  int fuse_delta, delta_cross, win_group;
+  // pair delta (gamma = 2R = 64 with 4 heads per group): tile A hands the four
+  // heads' delta rows to tile B through shared memory instead of the delta buffer
+  int delta_pair;
   float* anchor_delta_f32;      // optional fp32 dense - sparse per anchor (telemetry)
   __nv_bfloat16* out;           // [B, out_rows, H, d]
   int tma_out;                  // window launch: full tiles leave through tm_out (TMA stores)

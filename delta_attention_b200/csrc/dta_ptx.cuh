@@ -131,6 +131,23 @@ __device__ __forceinline__ bool mbar_poll(uint32_t bar, uint32_t parity, const W
   return mbar_poll_slow(bar, parity, w, code);
 }
 
+// Bounded wait until a shared-memory counter reaches `target` (same abort
+// protocol as mbar_wait).
+__device__ __forceinline__ bool smem_wait_geq(volatile int* c, int target, const WaitCtx& w, int code) {
+  if (*c >= target) return true;
+  const long long t0 = clock64();
+  while (*c < target) {
+    if (*w.abort_flag) return false;
+    if (clock64() - t0 > w.limit) {
+      *w.abort_flag = 1;
+      atomicCAS(w.err, 0, code);
+      return false;
+    }
+    __nanosleep(20);
+  }
+  return true;
+}
+
 // Programmatic dependent launch: the dependent grid's wait for the grid it
 // depends on (complete, writes visible), and the primary's early trigger.
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

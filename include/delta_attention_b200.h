@@ -118,10 +118,11 @@ typedef struct dta_prefill_args {
 /* Phases of dta_prefill.  ROWS: dense rows (anchors + tail) and sparse anchor
  * rows, written to the workspace (and anchor_delta when given).  WINDOW: the
  * windowed rows with the fused delta epilogue; it reads what a ROWS call with
- * identical arguments left in the same workspace.  With gamma == 64, uniform
- * anchors and 4 query heads per KV head, WINDOW forms the anchors' sparse rows
- * and dense - sparse itself (each 64-row window job starts at its anchor), so
- * ROWS computes dense rows only and anchor_delta is written by WINDOW. */
+ * identical arguments left in the same workspace.  With uniform anchors, 4 or
+ * 8 query heads per KV head and gamma a power of two >= 8, WINDOW forms each
+ * anchor's sparse row and dense - sparse itself (in the tile that holds the
+ * anchor row), so ROWS computes dense rows only and anchor_delta is written by
+ * WINDOW. */
 #define DTA_PHASE_ROWS 1
 #define DTA_PHASE_WINDOW 2
 

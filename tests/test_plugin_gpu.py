@@ -142,3 +142,38 @@ def test_log_drift_summary():
     st = m._drift_stats
     assert st["n"] == ((2048 - 128) // 64 - 1) * 8  # consecutive-anchor pairs x heads
     assert sum(st["hist"]) > 0 and -1.0 <= st["mean"] <= 1.0
+
+
+@pytest.mark.parametrize("policy,extra", [("drift", dict(drift_threshold=0.95)),
+                                          ("drift_rel", dict(drift_k=50.0))])
+def test_drift_refresh_policies_match_oracle(policy, extra):
+    """delta-mode decode with a drift-triggered refresh (``delta_attention/llama.py:586-606``):
+    the anchor decision needs this step's sparse row first, so the plug-in runs
+    the sparse pass, decides, and reads the dense row only on an anchor.  A
+    query sequence that drifts slowly and then jumps once must give the
+    oracle's anchor flags and outputs step by step."""
+    n0, T, H, Hkv, d = 4096, 14, 32, 8, 128
+    g = torch.Generator().manual_seed(11)
+    k = torch.randn(1, Hkv, n0 + T, d, generator=g).bfloat16()
+    v = torch.randn(1, Hkv, n0 + T, d, generator=g).bfloat16()
+    q0 = torch.randn(1, H, 1, d, generator=g)
+    dq = torch.randn(1, H, 1, d, generator=g)
+    jump = torch.randn(1, H, 1, d, generator=g)
+    qs = [((jump if t >= 11 else q0) + 0.02 * t * dq).bfloat16() for t in range(T)]
+    m = _module(decode_mode="delta", refresh_policy=policy, gamma_dec=64, gamma_dec_max=128,
+                sliding_window=1024, sink=128, **extra)
+    st = orc.OracleDecodeState()
+    flags, ref_flags = [], []
+    for t in range(T):
+        n = n0 + t
+        kc, vc = k[:, :, :n + 1], v[:, :, :n + 1]
+        out, _ = m.sdpa_rectangle_forward(m, qs[t].cuda(), kc.cuda(), vc.cuda(), scaling=d ** -0.5)
+        flags.append(m._dec_state["steps"] == 0)
+        ref, a = orc.delta_decode_step(st, qs[t].float(), kc.float(), vc.float(), window=1024, sink=128,
+                                       scaling=d ** -0.5, gamma_dec=64, refresh_policy=policy,
+                                       drift_k=extra.get("drift_k", 2.0),
+                                       drift_threshold=extra.get("drift_threshold", 0.95), gamma_dec_max=128)
+        ref_flags.append(a)
+        assert_close(out.cpu(), ref, f"{policy} step {t}")
+    assert flags == ref_flags, (flags, ref_flags)
+    assert flags[0] and flags[11] and sum(flags) == 2, flags  # first step and the jump

@@ -214,3 +214,22 @@ def test_rows_op_split_matches_dense_rows():
     out = ops.rows(q.cuda(), k.cuda(), v.cuda(), rows, rows, split_tiles=1, check=True)
     ref = orc.dense_rows(q.float(), k.float(), v.float(), rows, d ** -0.5)
     assert_close(out.cpu(), ref, "rows op, split per key tile")
+
+
+@pytest.mark.parametrize("G,gamma,s", [(4, 16, 1024), (4, 32, 1024), (4, 128, 1536), (4, 8, 1000),
+                                       (8, 64, 1024), (8, 16, 1024), (8, 32, 1280), (8, 128, 1536)])
+def test_fused_delta_all_strides_and_groups(G, gamma, s):
+    """Every fused-delta arrangement: anchors inside one warp's rows (gamma <= R),
+    in tile A for tile B (gamma = 2R), and over several consecutive jobs of one
+    CTA (gamma > 2R).  The fp32 telemetry the windowed launch writes must be the
+    oracle's dense minus sparse row at every anchor, and the output must match."""
+    Hkv, d, window, sink = 2, 128, 320, 48
+    H = G * Hkv
+    q, k, v = make_inputs(s, H, Hkv, d, seed=100 + G + gamma)
+    out, delta = _run(q, k, v, gamma=gamma, window=window, sink=sink, return_anchor_delta=True, check=True)
+    anchors, _, _ = orc.anchor_layout(s, gamma)
+    sc = d ** -0.5
+    qf, kf, vf = q.float(), k.float(), v.float()
+    ref = orc.dense_rows(qf, kf, vf, anchors, sc) - orc.sparse_rows(qf, kf, vf, anchors, window, sink, sc)
+    assert_close(delta.cpu(), ref, f"fused delta G={G} gamma={gamma}")
+    assert_close(out.cpu(), _oracle_full(q, k, v, gamma, window, sink), f"fused output G={G} gamma={gamma}")
