@@ -211,9 +211,11 @@ class DeltaDecoder:
         if a.qk_norm:  # Qwen3's _qkv hook
             q = rms_norm(q, layer["q_norm"], a.rms_eps)
             k = rms_norm(k, layer["k_norm"], a.rms_eps)
-        c, sn = cos[:, None, :], sin[:, None, :]
-        q = (q * c + rotate_half(q) * sn).to(self.dtype)
-        k = (k * c + rotate_half(k) * sn).to(self.dtype)
+        # RoPE in the activations' dtype with cos/sin rounded to it, as the
+        # reference's layers do (``delta_attention/llama.py:183-192``)
+        c, sn = cos[:, None, :].to(q.dtype), sin[:, None, :].to(q.dtype)
+        q = q * c + rotate_half(q) * sn
+        k = k * c + rotate_half(k) * sn
         # KV-cache write path: post-RoPE keys and values at positions [pos0, pos0 + s)
         kc, vc = self.k_cache[i], self.v_cache[i]
         kc[:, :, pos0:pos0 + s] = k.transpose(1, 2)
@@ -229,7 +231,7 @@ class DeltaDecoder:
             h = rms_norm(x, layer["norm2"], a.rms_eps)
             gu = h @ layer["w_gu"].t()
             g, u = gu.split(self.Il, dim=-1)
-            m = (torch.nn.functional.silu(g.float()) * u.float()).to(self.dtype) @ layer["w_down"].t()
+            m = (torch.nn.functional.silu(g) * u) @ layer["w_down"].t()
         with self._timed("all_reduce"):
             x = x + self.tp.all_reduce(m)
         return x

@@ -290,6 +290,24 @@ def rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_rows: torch.Tensor
     return out if odt == torch.bfloat16 else out.to(odt)
 
 
+_decode_ws = {}
+
+
+def _decode_workspace(nbytes: int, device) -> torch.Tensor:
+    """Decode workspace kept per (device, stream) and grown on demand: decode
+    runs once per layer and token, so a fresh allocation per call would cost
+    more host time than the kernel.  Calls on one stream are ordered, so they
+    may share it.  (During CUDA graph capture a private buffer is used.)"""
+    if torch.cuda.is_current_stream_capturing():
+        return _workspace(nbytes, device)
+    key = (_device_index(device), _stream())
+    ws = _decode_ws.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = _workspace(nbytes, device)
+        _decode_ws[key] = ws
+    return ws
+
+
 def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, window: int, sink: int,
            scaling: Optional[float] = None, want_dense: bool = True, want_sparse: bool = True,
            n_keys: Optional[int] = None) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor]]:
@@ -318,7 +336,7 @@ def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, window: int, si
     a.scaling = float(scaling)
     a.window, a.sink = int(window), int(sink)
     a.dense_out, a.sparse_out = _ptr(dense), _ptr(sparse)
-    ws = _workspace(lib().dta_decode_workspace_size(ctypes.byref(a)), q.device)
+    ws = _decode_workspace(lib().dta_decode_workspace_size(ctypes.byref(a)), q.device)
     a.workspace, a.workspace_bytes = _ptr(ws), ws.numel()
     _check_status(lib().dta_decode(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_decode")
     return dense, sparse
