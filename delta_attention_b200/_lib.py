@@ -81,6 +81,7 @@ class PrefillArgs(ctypes.Structure):
         ("phases", c_i32),
         ("workspace", c_vp), ("workspace_bytes", ctypes.c_size_t),
         ("error_word", c_vp), ("wait_cycles", c_i64), ("flags", c_i32), ("split_tiles", c_i32),
+        ("anchor_delta_in", c_vp),
     ]
 
 

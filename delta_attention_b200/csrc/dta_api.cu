@@ -197,8 +197,10 @@ int prefill_layout(const dta_prefill_args* a, int sms, PrefillLayout* L) {
     if (a->n_anchors <= 0 || a->s_p <= 0 || a->s_p > s || a->n_anchors > a->s_p) return DTA_ERR_INVALID_ARG;
     L->s_p = a->s_p;
     L->n_anchor = a->n_anchors;
-    L->n_sel = a->n_anchors + (s - a->s_p);
+    // with the anchors' deltas given, the rows launch computes the tail only
+    L->n_sel = (a->anchor_delta_in ? 0 : a->n_anchors) + (s - a->s_p);
   } else {
+    if (a->anchor_delta_in) return DTA_ERR_INVALID_ARG;  // only with explicit anchors
     if (a->gamma <= 0) return DTA_ERR_GAMMA;
     const int cut_n = s % a->gamma + (a->gamma > 128 ? a->gamma : 128);
     const int s_p = s - cut_n;
@@ -217,12 +219,14 @@ int prefill_layout(const dta_prefill_args* a, int sms, PrefillLayout* L) {
   L->fuse = a->mode == DTA_MODE_DELTA && !a->anchors && L->n_anchor > 0 && (G == 4 || G == 8) && pow2;
   L->delta_cross = L->fuse && a->gamma > R;
   L->win_group = (L->fuse && a->gamma > JR) ? a->gamma / JR : 1;
-  L->n_sparse_tiles = (a->mode == DTA_MODE_DELTA && !L->fuse) ? (L->n_anchor + JR - 1) / JR : 0;
+  const bool have_delta = a->anchor_delta_in != nullptr;
+  if (have_delta && (a->mode != DTA_MODE_DELTA || a->anchor_delta)) return DTA_ERR_INVALID_ARG;
+  L->n_sparse_tiles = (a->mode == DTA_MODE_DELTA && !L->fuse && !have_delta) ? (L->n_anchor + JR - 1) / JR : 0;
   if (L->n_sel > 0) {
     // a sparse anchor tile spans its rows' window plus the rows' own spread
     const long long sparse_tiles =
         (long long)L->n_sparse_tiles * BG * ((a->window + a->sink) / dta::PREFILL_BN + 2);
-    const int n_anchor = L->n_anchor, s_p = L->s_p, n_sel = L->n_sel, gamma = a->gamma;
+    const int n_anchor = have_delta ? 0 : L->n_anchor, s_p = L->s_p, n_sel = L->n_sel, gamma = a->gamma;
     const bool uniform = !a->anchors;
     auto tiles_of = [&](int t) {
       const int i = (t + 1) * JR < n_sel ? (t + 1) * JR - 1 : n_sel - 1;  // last list row of tile t
@@ -236,7 +240,7 @@ int prefill_layout(const dta_prefill_args* a, int sms, PrefillLayout* L) {
   } else {
     L->split = RowsSplit();
   }
-  const bool need_bufs = a->mode == DTA_MODE_DELTA && L->n_anchor > 0;
+  const bool need_bufs = a->mode == DTA_MODE_DELTA && L->n_anchor > 0 && !have_delta;
   L->buf_bytes = need_bufs ? align_up((size_t)a->batch * L->n_anchor * a->n_heads * a->head_dim * 4, 256) : 0;
   L->delta_bytes = need_bufs ? align_up((size_t)a->batch * L->n_anchor * a->n_heads * a->head_dim * 2, 256) : 0;
   L->ws_bytes = kHeaderBytes + L->split.cnt_bytes + 2 * L->buf_bytes + L->delta_bytes + L->split.part_o_bytes +
@@ -288,6 +292,7 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
       !stride_ok(a->v_stride_s) || !stride_ok(a->v_stride_h) || !stride_ok(a->v_stride_b))
     return DTA_ERR_STRIDE;
   if (a->anchor_delta && (a->mode != DTA_MODE_DELTA || !aligned16(a->anchor_delta))) return DTA_ERR_INVALID_ARG;
+  if (a->anchor_delta_in && !aligned16(a->anchor_delta_in)) return DTA_ERR_ALIGNMENT;
   if (a->phases < 0 || a->phases > (DTA_PHASE_ROWS | DTA_PHASE_WINDOW)) return DTA_ERR_INVALID_ARG;
   if (a->wait_cycles < 0 || (a->flags & ~DTA_FLAG_TEST_STALL) != 0) return DTA_ERR_INVALID_ARG;
   if (a->error_word && ((uintptr_t)a->error_word & 3u) != 0) return DTA_ERR_ALIGNMENT;
@@ -328,7 +333,8 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   p.sparse_buf = L.buf_bytes ? reinterpret_cast<float*>(cur + L.buf_bytes) : nullptr;
   cur += 2 * L.buf_bytes;
   __nv_bfloat16* delta_buf = L.delta_bytes ? reinterpret_cast<__nv_bfloat16*>(cur) : nullptr;
-  p.delta_buf = delta_buf;
+  // given deltas (explicit anchors) replace the delta kernel's output
+  p.delta_buf = a->anchor_delta_in ? reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(a->anchor_delta_in)) : delta_buf;
   cur += L.delta_bytes;
   p.part_o = L.split.part_o_bytes ? reinterpret_cast<float*>(cur) : nullptr;
   cur += L.split.part_o_bytes;
@@ -356,6 +362,13 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
     dta::PrefillParams r = p;
     r.launch = dta::LAUNCH_ROWS;
     r.direct_from = (a->mode == DTA_MODE_DELTA) ? L.n_anchor : 0;
+    if (a->anchor_delta_in) {
+      // the anchors' deltas are given: the list is the dense tail alone, every
+      // row of it stored to out at position s_p + index
+      r.n_anchor = 0;
+      r.anchors = nullptr;
+      r.direct_from = 0;
+    }
     r.n_dense_tiles = L.split.n_dense_tiles;
     r.n_sparse_tiles = L.n_sparse_tiles;
     r.split_c = L.split.c;

@@ -121,7 +121,7 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
             return_anchor_delta: bool = False, workspace: Optional[torch.Tensor] = None,
             phases: int = 0, out: Optional[torch.Tensor] = None, check: bool = False,
             validate: bool = True, wait_cycles: int = 0, flags: int = 0, split_tiles: int = 0,
-            use_error_word: bool = True):
+            use_error_word: bool = True, anchor_delta_in: Optional[torch.Tensor] = None):
     """Delta-attention prefill of one layer.
 
     q [b, H, s, d], k/v [b, Hkv, s, d] (post-RoPE; any strides with d
@@ -134,6 +134,9 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
     :func:`check_errors`); ``wait_cycles``, ``flags`` and ``split_tiles`` are
     the C ABI's (0 = defaults).  With ``use_error_word=False`` kernel codes go
     to the workspace header instead (read with :func:`check_workspace`).
+    ``anchor_delta_in`` [b, n_anchors, H, d] (explicit anchors only): the
+    anchors' dense - sparse rows computed earlier; only the dense tail rows
+    are then computed again.
     """
     _check_cuda(q, k, v)
     odt = q.dtype
@@ -164,6 +167,8 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
     a.phases = int(phases)
     a.split_tiles = int(split_tiles)
     anc = None
+    if anchor_delta_in is not None and anchors is None:
+        raise ValueError("anchor_delta_in needs explicit anchors")
     if anchors is not None:
         if s_p is None:
             raise ValueError("explicit anchors need s_p")
@@ -171,6 +176,11 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
             _validate_anchors(anchors, int(s_p), s)
         anc = anchors.to(device=q.device, dtype=torch.int32).contiguous()
         a.anchors = _ptr(anc)
+        if anchor_delta_in is not None:
+            if tuple(anchor_delta_in.shape) != (b, anc.numel(), H, d):
+                raise ValueError(f"anchor_delta_in must be [{b}, {anc.numel()}, {H}, {d}]")
+            din = anchor_delta_in.to(device=q.device, dtype=torch.bfloat16).contiguous()
+            a.anchor_delta_in = _ptr(din)
         a.n_anchors = anc.numel()
         a.s_p = int(s_p)
     ws_bytes = lib().dta_prefill_workspace_size(ctypes.byref(a))

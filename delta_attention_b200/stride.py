@@ -5,9 +5,10 @@ rules ``next_gamma`` / ``next_gamma_relative`` ``:55-86``, chunking ``:111-112``
 cost model ``:89-128``) and drives the kernels for the chunked adaptive
 placement of ``delta_attention/llama.py:759-824``: per chunk, the anchor
 deltas come from the prefill's row launch (``ops.anchor_deltas``); the final
-output is one ``ops.prefill`` call with the chosen anchor list, whose windowed
-launch applies the variable-stride broadcast (row i gets the delta of the
-nearest anchor <= i, ``delta_attention/stride.py:26-40``) in its epilogue.
+output is one ``ops.prefill`` call with the chosen anchor list and those
+deltas (so no anchor row is computed twice), whose windowed launch applies
+the variable-stride broadcast (row i gets the delta of the nearest anchor <= i,
+``delta_attention/stride.py:26-40``) in its epilogue.
 """
 
 from __future__ import annotations
@@ -92,12 +93,13 @@ def adaptive_prefill(cfg, q, k, v, scaling, layer_idx: int = 0):
     gamma_c = gamma0
     trigger = getattr(cfg, "stride_trigger", "absolute")
     history: List[float] = []
-    parts, log = [], []
+    parts, deltas, log = [], [], []
     for start, end in plan_chunks(s_p, int(cfg.adapt_chunk)):
         c_idx = torch.arange(start, end, gamma_c, device=q.device)
         delta = ops.anchor_deltas(q, k, v, c_idx, window=window, sink=sink, scaling=scaling, q_block=q_block)
         cos_mean, cos_min = interanchor_cos(delta)
         parts.append(c_idx)
+        deltas.append(delta)
         log.append({"start": int(start), "gamma": int(gamma_c), "cos_mean": cos_mean, "cos_min": cos_min,
                     "n_anchors": int(c_idx.numel())})
         if trigger == "relative":
@@ -108,8 +110,10 @@ def adaptive_prefill(cfg, q, k, v, scaling, layer_idx: int = 0):
             gamma_c = next_gamma(cos_mean, gamma_c, threshold=float(cfg.adapt_threshold),
                                  gamma_min=int(cfg.gamma_min), gamma_max=int(cfg.gamma_max))
     idx = torch.cat(parts)
+    # the chunks' anchor deltas are reused: the final call computes only the
+    # dense tail rows and the windowed rows (delta_attention/llama.py:784-810)
     out = ops.prefill(q, k, v, gamma=gamma0, window=window, sink=sink, scaling=scaling, mode="delta",
-                      q_block=q_block, anchors=idx, s_p=s_p)
+                      q_block=q_block, anchors=idx, s_p=s_p, anchor_delta_in=torch.cat(deltas, dim=1))
     tail = torch.arange(s_p, s)
     stats: Dict[str, Any] = {
         "kind": "stride", "layer": int(layer_idx), "seq_len": int(s),

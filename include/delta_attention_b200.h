@@ -106,6 +106,10 @@ typedef struct dta_prefill_args {
                              from the device's SM count and the total work.  A dense row tile
                              longer than this runs as several chunks whose partial results the
                              last-finishing chunk merges (log-sum-exp); see dta_prefill_workspace_size */
+  const void* anchor_delta_in; /* optional device bf16 [batch, n_anchors, n_heads, head_dim] with explicit
+                             anchors, delta mode: dense - sparse of every anchor row, computed earlier
+                             (the adaptive stride planner has it); the ROWS phase then computes only
+                             the dense tail rows and WINDOW applies these rows */
 } dta_prefill_args;
 
 /* Test hook: the producer warp of every CTA first waits on a barrier that

@@ -155,3 +155,12 @@ def test_ops_refuse_cpu_tensors():
     k = torch.zeros(1, 1, 256, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         ops.prefill(q, k, k, gamma=64, window=64, sink=16)
+
+
+def test_anchor_delta_in_needs_explicit_anchors():
+    L = _lib.lib()
+    a = _prefill_args()
+    a.workspace, a.workspace_bytes = 1 << 20, 1 << 30
+    a.anchor_delta_in = 1 << 21  # uniform anchors: refused
+    assert L.dta_prefill(ctypes.byref(a), None) == 1
+    assert L.dta_prefill_workspace_size(ctypes.byref(a)) == 0
