@@ -187,6 +187,22 @@ class _PadSeq:
         return self
 
 
+def cpu_calibration():
+    """The committed record (tests/golden/cpu_timing.json, written by
+    tests/golden/make_golden.py --timing-only where the reference checkout
+    exists) of the reference's own CPU path against the oracle port on one
+    host: the port is the CPU baseline timed here, and this says how its speed
+    relates to the reference's own code.  None when the record is absent."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden", "cpu_timing.json")
+    try:
+        with open(path) as f:
+            rec = json.load(f)
+    except (OSError, ValueError):
+        return None
+    return {k: rec[k] for k in ("what", "reference", "host_cpu", "threads", "reference_tokens_per_s",
+                                "port_tokens_per_s", "port_over_reference") if k in rec}
+
+
 def cpu_baseline(args, seconds):
     """Time the oracle on a row sample near N/2 sized to ~``seconds`` of CPU work.
     Returns (tokens/s, threads, description)."""
@@ -243,7 +259,8 @@ def run_reference(args, rank, world):
         "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1)*0.5, RoPE theta 5e5)",
         "config": workload_config(args, world),
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample,
+                         "calibration": cpu_calibration()},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -260,9 +277,21 @@ def physical_gpu(local_rank: int) -> str:
     return str(local_rank)
 
 
+def workload_name(args):
+    """The benchmark matrix entry the shapes belong to (config 2: Llama-3.1-8B
+    attention, 32/8 heads, W=2048; config 5: Llama-3.1-70B attention, 64/8
+    heads, W=4096), else a plain description of the shapes."""
+    if (args.heads, args.kv_heads, args.head_dim, args.window, args.sink) == (32, 8, 128, 2048, 128):
+        return "config2: single-layer delta-attention prefill, Llama-3.1-8B attention shapes"
+    if (args.heads, args.kv_heads, args.head_dim, args.window, args.sink, args.gamma) == (64, 8, 128, 4096, 128, 64):
+        return "config5: single-layer delta-attention prefill, Llama-3.1-70B attention shapes"
+    return (f"single-layer delta-attention prefill, {args.heads}/{args.kv_heads} heads, d={args.head_dim}, "
+            f"W={args.window}, S={args.sink}")
+
+
 def workload_config(args, world):
     return {
-        "workload": "config2: single-layer delta-attention prefill, Llama-3.1-8B attention shapes",
+        "workload": workload_name(args),
         "seq_len": args.seq, "n_heads": args.heads, "n_kv_heads": args.kv_heads, "head_dim": args.head_dim,
         "window": args.window, "sink": args.sink, "gamma": args.gamma, "sequences_per_gpu":
             (1 if args.scaling == "weak" else 1.0 / world), "partition": "kv-group units",
@@ -524,7 +553,8 @@ def run_b200(args, rank, world, local_rank):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         val, cores, desc = cpu_baseline(args, args.cpu_seconds)
-        cpu = {"value": val, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc}
+        cpu = {"value": val, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc,
+               "calibration": cpu_calibration()}
 
     if rank == 0:
         line = {

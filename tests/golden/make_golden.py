@@ -229,16 +229,70 @@ def gen_decode(ref: str, out_dir: str) -> None:
     print("[golden] decode_reference", rec, flush=True)
 
 
+def gen_cpu_timing(ref: str, out_dir: str, repeats: int = 2) -> None:
+    """Time the reference's own CPU path (``delta_forward_train``, eager
+    FlexAttention, fp32) against this repository's CPU oracle port on the same
+    config-1 input, same host and thread count.  The GPU box has no reference
+    checkout, so the benchmark's reference arm times the port; this record
+    relates the two (``port_over_reference`` = port tokens/s / reference tokens/s)."""
+    import platform
+
+    from oracle import delta_oracle as orc
+
+    flex_delta = load_flex(ref)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    s, H, Hkv, d, gamma, window, sink, theta, seed, _ = FLEX_CASES["flex_config1"]
+    q, k, v = make_inputs(s, H, Hkv, d, seed=seed, rope_theta=theta, dtype=torch.bfloat16)
+
+    def best(fn):
+        ts = []
+        for _ in range(repeats):
+            t0 = time.perf_counter()
+            with torch.no_grad():
+                fn()
+            ts.append(time.perf_counter() - t0)
+        return min(ts)
+
+    t_ref = best(lambda: flex_delta.delta_forward_train(q.float(), k.float(), v.float(), gamma=gamma,
+                                                          window=window, sink=sink))
+    t_port = best(lambda: orc.delta_forward(q, k, v, gamma, window, sink, dtype=torch.float32))
+    cpu = platform.processor() or platform.machine()
+    try:
+        with open("/proc/cpuinfo") as f:
+            cpu = next((ln.split(":", 1)[1].strip() for ln in f if ln.startswith("model name")), cpu)
+    except OSError:
+        pass
+    rec = {
+        "what": "whole config-1 layer (s=4096, 32/8 heads, d=128, W=1024, S=64, gamma=64), fp32 on CPU, best of "
+                f"{repeats}",
+        "reference": "delta_attention/train/flex_delta.py delta_forward_train (eager flex_attention)",
+        "port": "oracle/delta_oracle.py delta_forward (dtype float32)",
+        "host_cpu": cpu, "threads": threads, "torch": torch.__version__,
+        "reference_s": t_ref, "port_s": t_port,
+        "reference_tokens_per_s": s / t_ref, "port_tokens_per_s": s / t_port,
+        "port_over_reference": t_ref / t_port,
+    }
+    with open(os.path.join(out_dir, "cpu_timing.json"), "w") as f:
+        json.dump(rec, f, indent=1)
+    print("[golden] cpu_timing", rec, flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("DTA_REFERENCE"),
                     help="path of the reference checkout (or set DTA_REFERENCE)")
     ap.add_argument("--only", nargs="*")
+    ap.add_argument("--timing-only", action="store_true",
+                    help="only write cpu_timing.json (reference CPU path vs the oracle port)")
     args = ap.parse_args()
     if not args.reference:
         raise SystemExit("pass --reference <checkout> or set DTA_REFERENCE")
     if not os.path.isdir(args.reference):
         raise SystemExit(f"reference checkout not found at {args.reference}")
+    if args.timing_only:
+        gen_cpu_timing(args.reference, HERE)
+        return
     gen_stride(args.reference, HERE)
     gen_decode(args.reference, HERE)
     gen_flex(args.reference, HERE, args.only)
