@@ -14,7 +14,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("DTA_LIBRARY") or os.path.join(_HERE, "_lib", "libdelta_attention_b200.so")
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 DTA_OK = 0
 STATUS_NAMES = {
@@ -59,6 +59,8 @@ EXPORTED = (
     "dta_status_string",
     "dta_last_cuda_error",
     "dta_check_workspace",
+    "dta_backward_workspace_size",
+    "dta_backward",
 )
 
 c_i32 = ctypes.c_int32
@@ -82,6 +84,7 @@ class PrefillArgs(ctypes.Structure):
         ("workspace", c_vp), ("workspace_bytes", ctypes.c_size_t),
         ("error_word", c_vp), ("wait_cycles", c_i64), ("flags", c_i32), ("split_tiles", c_i32),
         ("anchor_delta_in", c_vp),
+        ("lse_sparse", c_vp), ("lse_dense", c_vp),
     ]
 
 
@@ -117,6 +120,24 @@ class DecodeArgs(ctypes.Structure):
         ("window", c_i32), ("sink", c_i32),
         ("dense_out", c_vp), ("sparse_out", c_vp),
         ("workspace", c_vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class BackwardArgs(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", c_i32),
+        ("batch", c_i32), ("n_heads", c_i32), ("n_kv_heads", c_i32), ("seq_len", c_i32), ("head_dim", c_i32),
+        ("q", c_vp), ("q_stride_b", c_i64), ("q_stride_h", c_i64), ("q_stride_s", c_i64),
+        ("k", c_vp), ("k_stride_b", c_i64), ("k_stride_h", c_i64), ("k_stride_s", c_i64),
+        ("v", c_vp), ("v_stride_b", c_i64), ("v_stride_h", c_i64), ("v_stride_s", c_i64),
+        ("out", c_vp), ("grad_out", c_vp),
+        ("anchor_delta", c_vp), ("lse_sparse", c_vp), ("lse_dense", c_vp),
+        ("grad_q", c_vp), ("grad_k", c_vp), ("grad_v", c_vp),
+        ("scaling", ctypes.c_float),
+        ("gamma", c_i32), ("window", c_i32), ("sink", c_i32), ("q_block", c_i32),
+        ("delta_grad_scale", ctypes.c_float),
+        ("workspace", c_vp), ("workspace_bytes", ctypes.c_size_t),
+        ("error_word", c_vp), ("wait_cycles", c_i64),
     ]
 
 
@@ -168,6 +189,10 @@ def lib() -> ctypes.CDLL:
         L.dta_last_cuda_error.restype = ctypes.c_int
         L.dta_check_workspace.argtypes = [c_vp, c_vp, ctypes.POINTER(ctypes.c_int)]
         L.dta_check_workspace.restype = ctypes.c_int
+        L.dta_backward_workspace_size.argtypes = [ctypes.POINTER(BackwardArgs)]
+        L.dta_backward_workspace_size.restype = ctypes.c_size_t
+        L.dta_backward.argtypes = [ctypes.POINTER(BackwardArgs), c_vp]
+        L.dta_backward.restype = ctypes.c_int
         if L.dta_abi_version() != ABI_VERSION:
             raise RuntimeError("delta_attention_b200 library ABI mismatch")
         _lib = L

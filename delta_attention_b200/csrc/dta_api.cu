@@ -39,6 +39,11 @@ int check_device(int* sms) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail_cuda(e);
   if (dev < 0 || dev >= 64) return DTA_ERR_UNSUPPORTED_DEVICE;
+  // Make the device's primary context current on this thread: the TMA
+  // descriptor encode is a driver call that needs a current context, which a
+  // host thread that has made no context-creating runtime call yet (a fresh
+  // worker thread) does not have.
+  if ((e = cudaSetDevice(dev)) != cudaSuccess) return fail_cuda(e);
   std::lock_guard<std::mutex> lock(mu);
   if (info[dev].ok < 0) {
     int major = 0, n = 0;
@@ -53,22 +58,11 @@ int check_device(int* sms) {
   return DTA_OK;
 }
 
-}  // namespace dta
-
-namespace {
-
-constexpr size_t kHeaderBytes = 256;  // job counter, error word
-
-inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
-
-using dta::check_device;
-using dta::fail_cuda;
-
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-EncodeTiledFn get_encode_fn() {
+static EncodeTiledFn get_encode_fn() {
   static EncodeTiledFn fn = nullptr;
   if (!fn) {
     void* ptr = nullptr;
@@ -84,7 +78,10 @@ EncodeTiledFn get_encode_fn() {
 int encode_4d(CUtensorMap* map, const void* base, int d, long long rows, int heads, int batch, long long s_row,
               long long s_head, long long s_batch, int box_rows, int box_heads) {
   EncodeTiledFn fn = get_encode_fn();
-  if (!fn) return DTA_ERR_CUDA;
+  if (!fn) {
+    g_last_cuda_error = (int)CUDA_ERROR_NOT_FOUND;
+    return DTA_ERR_CUDA;
+  }
   cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)rows, (cuuint64_t)heads, (cuuint64_t)batch};
   cuuint64_t strides[3] = {(cuuint64_t)(s_row * 2), (cuuint64_t)(s_head * 2), (cuuint64_t)(s_batch * 2)};
   cuuint32_t box[4] = {64u, (cuuint32_t)box_rows, (cuuint32_t)box_heads, 1u};
@@ -92,8 +89,23 @@ int encode_4d(CUtensorMap* map, const void* base, int d, long long rows, int hea
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? DTA_OK : DTA_ERR_CUDA;
+  if (r == CUDA_SUCCESS) return DTA_OK;
+  g_last_cuda_error = (int)r;  // the driver's CUresult, reported by dta_last_cuda_error
+  return DTA_ERR_CUDA;
 }
+
+}  // namespace dta
+
+namespace {
+
+constexpr size_t kHeaderBytes = 256;  // job counter, error word
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+using dta::check_device;
+using dta::fail_cuda;
+
+using dta::encode_4d;
 
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 inline bool stride_ok(long long s) { return s > 0 && (s * 2) % 16 == 0; }
@@ -296,6 +308,10 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   if (a->phases < 0 || a->phases > (DTA_PHASE_ROWS | DTA_PHASE_WINDOW)) return DTA_ERR_INVALID_ARG;
   if (a->wait_cycles < 0 || (a->flags & ~DTA_FLAG_TEST_STALL) != 0) return DTA_ERR_INVALID_ARG;
   if (a->error_word && ((uintptr_t)a->error_word & 3u) != 0) return DTA_ERR_ALIGNMENT;
+  if ((a->lse_sparse && ((uintptr_t)a->lse_sparse & 3u) != 0) || (a->lse_dense && ((uintptr_t)a->lse_dense & 3u) != 0))
+    return DTA_ERR_ALIGNMENT;
+  // the dense rows' log-sum-exp is indexed by the full list (anchors, tail)
+  if (a->lse_dense && a->anchor_delta_in) return DTA_ERR_INVALID_ARG;
   const int phases = a->phases ? a->phases : (DTA_PHASE_ROWS | DTA_PHASE_WINDOW);
   int sms = 0;
   if ((st = check_device(&sms)) != DTA_OK) return st;
@@ -323,6 +339,8 @@ int dta_prefill(const dta_prefill_args* a, void* stream_) {
   p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
   p.wait_cycles = a->wait_cycles > 0 ? a->wait_cycles : dta::kWaitTimeoutCycles;
   p.test_stall = (a->flags & DTA_FLAG_TEST_STALL) ? 1 : 0;
+  p.lse_sparse = a->lse_sparse;
+  p.lse_dense = a->lse_dense;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
   p.counter = reinterpret_cast<int*>(ws);
   p.error = a->error_word ? a->error_word : reinterpret_cast<int*>(ws) + 1;

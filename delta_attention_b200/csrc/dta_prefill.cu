@@ -797,6 +797,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
       }
       // 1/l to ~2 ulp (__fdividef): far below the bf16 rounding of the output
       const float inv_l = (l_run > 0.f) ? __fdividef(1.f, l_run) : 0.f;
+      // the windowed row's base-2 log-sum-exp, kept by the training forward
+      if (WIN && p.lse_sparse && row_valid)
+        p.lse_sparse[((long long)J.b * p.H + h) * p.seq_q + qpos] = (l_run > 0.f) ? m_run + __log2f(l_run) : -INFINITY;
       if (WIN && !dep_done) {
         // the rows launch (the grid this one may overlap) has completed and its
         // writes are visible before the first read of its output.  Its output
@@ -892,6 +895,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
           }
         }
         const float inv_w = (wsum > 0.f) ? __fdividef(1.f, wsum) : 0.f;
+        if (p.lse_dense && row_valid && J.kind == JOB_DENSE_ROWS)
+          p.lse_dense[((long long)J.b * p.H + h) * p.n_sel + gli] = (wsum > 0.f) ? M + __log2f(wsum) : -INFINITY;
         __nv_bfloat16* dbf = (store && mode_out == 0)
                                  ? p.out + (((long long)J.b * p.out_rows + out_row) * p.H + h) * HD
                                  : nullptr;
@@ -943,6 +948,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_kernel(const __grid_co
         }
         continue;
       }
+      // the dense row's base-2 log-sum-exp, kept by the training forward
+      if (p.lse_dense && row_valid && J.kind == JOB_DENSE_ROWS)
+        p.lse_dense[((long long)J.b * p.H + h) * p.n_sel + gli] = (l_run > 0.f) ? m_run + __log2f(l_run) : -INFINITY;
       }  // !WIN
       const uint64_t inv2 = f2_pack(inv_l, inv_l);
       __nv_bfloat16* dst_bf = (store && mode_out == 0)

@@ -80,6 +80,11 @@ struct PrefillParams {
   long long wait_cycles;        // budget of each bounded wait (clock64 cycles, > 0)
   int test_stall;               // test hook: the producer first waits on a barrier nothing completes
   int seq_q, kv_len;            // rows of q and of k/v: bounds for explicit row lists
+  // optional base-2 log-sum-exp of every produced row (training forward):
+  // windowed rows into lse_sparse[(b * H + h) * seq_q + row], dense rows of the
+  // rows launch into lse_dense[(b * H + h) * n_sel + list index]
+  float* lse_sparse;
+  float* lse_dense;
 };
 
 // Multiplier and shift with n / d == (n * mul) >> sh for every 0 <= n < 2^31

@@ -20,7 +20,7 @@ from typing import Optional, Tuple
 import torch
 
 from . import _lib
-from ._lib import ABI_VERSION, KERNEL_CODES, DecodeArgs, DtaError, PrefillArgs, RowsArgs, lib
+from ._lib import ABI_VERSION, KERNEL_CODES, BackwardArgs, DecodeArgs, DtaError, PrefillArgs, RowsArgs, lib
 from ._lib import check as _check_status
 
 DTA_ERR_KERNEL_TIMEOUT = 10
@@ -121,7 +121,8 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
             return_anchor_delta: bool = False, workspace: Optional[torch.Tensor] = None,
             phases: int = 0, out: Optional[torch.Tensor] = None, check: bool = False,
             validate: bool = True, wait_cycles: int = 0, flags: int = 0, split_tiles: int = 0,
-            use_error_word: bool = True, anchor_delta_in: Optional[torch.Tensor] = None):
+            use_error_word: bool = True, anchor_delta_in: Optional[torch.Tensor] = None,
+            lse_sparse: Optional[torch.Tensor] = None, lse_dense: Optional[torch.Tensor] = None):
     """Delta-attention prefill of one layer.
 
     q [b, H, s, d], k/v [b, Hkv, s, d] (post-RoPE; any strides with d
@@ -137,6 +138,10 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
     ``anchor_delta_in`` [b, n_anchors, H, d] (explicit anchors only): the
     anchors' dense - sparse rows computed earlier; only the dense tail rows
     are then computed again.
+    ``lse_sparse`` [b, H, s] and ``lse_dense`` [b, H, n_sel] (fp32, contiguous,
+    optional) receive the base-2 log-sum-exp of every windowed row (rows below
+    s_p) and of every dense row (anchors, then the tail), which the training
+    backward needs.
     """
     _check_cuda(q, k, v)
     odt = q.dtype
@@ -194,6 +199,13 @@ def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, gamma: int, wi
     a.error_word = _ptr(error_word(q.device)) if use_error_word else None
     a.wait_cycles = int(wait_cycles)
     a.flags = int(flags)
+    for name, t in (("lse_sparse", lse_sparse), ("lse_dense", lse_dense)):
+        if t is not None:
+            if t.dtype != torch.float32 or not t.is_contiguous() or t.device != q.device:
+                raise ValueError(f"{name} must be a contiguous fp32 tensor on {q.device}")
+            setattr(a, name, _ptr(t))
+    if lse_sparse is not None and tuple(lse_sparse.shape) != (b, H, s):
+        raise ValueError(f"lse_sparse must be [{b}, {H}, {s}]")
     delta = None
     if return_anchor_delta and mode == "delta":
         if anc is not None:
@@ -350,6 +362,64 @@ def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, window: int, si
     a.workspace, a.workspace_bytes = _ptr(ws), ws.numel()
     _check_status(lib().dta_decode(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_decode")
     return dense, sparse
+
+
+def backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, grad_out: torch.Tensor,
+             anchor_delta: torch.Tensor, lse_sparse: torch.Tensor, lse_dense: torch.Tensor, *, gamma: int,
+             window: int, sink: int, scaling: Optional[float] = None, q_block: int = 64,
+             delta_grad_scale: float = 1.0, check: bool = False, wait_cycles: int = 0):
+    """Gradients (dq, dk, dv), bf16, of the delta-attention layer with uniform
+    anchors (``dta_backward``): q [b, H, s, d], k/v [b, Hkv, s, d] and the
+    forward's ``out`` [b, s, H, d], fp32 ``anchor_delta`` [b, n_anchor, H, d],
+    ``lse_sparse`` [b, H, s] and ``lse_dense`` [b, H, n_sel] (from
+    :func:`prefill` with the same parameters); ``grad_out`` [b, s, H, d].
+    ``delta_grad_scale`` multiplies the gradient through the broadcast delta
+    (0 = the delta detached)."""
+    _check_cuda(q, k, v, out, grad_out, anchor_delta, lse_sparse, lse_dense)
+    qb, kb, vb = _bf16_lastdim_contig(q), _bf16_lastdim_contig(k), _bf16_lastdim_contig(v)
+    b, H, s, d = qb.shape
+    Hkv = kb.shape[1]
+    if kb.shape != (b, Hkv, s, d) or vb.shape != kb.shape:
+        raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
+    if tuple(out.shape) != (b, s, H, d) or tuple(grad_out.shape) != (b, s, H, d):
+        raise ValueError("out and grad_out must be [b, s, H, d]")
+    if scaling is None:
+        scaling = d ** -0.5
+    ob = out.to(torch.bfloat16).contiguous()
+    gb = grad_out.to(torch.bfloat16).contiguous()
+    ad = anchor_delta.to(torch.float32).contiguous()
+    ls = lse_sparse.to(torch.float32).contiguous()
+    ld = lse_dense.to(torch.float32).contiguous()
+    dq = torch.empty(b, H, s, d, dtype=torch.bfloat16, device=q.device)
+    dk = torch.empty(b, Hkv, s, d, dtype=torch.bfloat16, device=q.device)
+    dv = torch.empty_like(dk)
+    a = BackwardArgs()
+    a.abi_version = ABI_VERSION
+    a.batch, a.n_heads, a.n_kv_heads, a.seq_len, a.head_dim = b, H, Hkv, s, d
+    a.q = _ptr(qb)
+    a.q_stride_b, a.q_stride_h, a.q_stride_s = _strides(qb)
+    a.k = _ptr(kb)
+    a.k_stride_b, a.k_stride_h, a.k_stride_s = _strides(kb)
+    a.v = _ptr(vb)
+    a.v_stride_b, a.v_stride_h, a.v_stride_s = _strides(vb)
+    a.out, a.grad_out = _ptr(ob), _ptr(gb)
+    a.anchor_delta, a.lse_sparse, a.lse_dense = _ptr(ad), _ptr(ls), _ptr(ld)
+    a.grad_q, a.grad_k, a.grad_v = _ptr(dq), _ptr(dk), _ptr(dv)
+    a.scaling = float(scaling)
+    a.gamma, a.window, a.sink, a.q_block = int(gamma), int(window), int(sink), int(q_block)
+    a.delta_grad_scale = float(delta_grad_scale)
+    ws_bytes = lib().dta_backward_workspace_size(ctypes.byref(a))
+    if ws_bytes == 0:
+        _check_status(lib().dta_backward(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_backward")
+    workspace = _workspace(ws_bytes, q.device)
+    a.workspace = _ptr(workspace)
+    a.workspace_bytes = workspace.numel()
+    a.error_word = _ptr(error_word(q.device))
+    a.wait_cycles = int(wait_cycles)
+    _check_status(lib().dta_backward(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_backward")
+    if check:
+        check_errors(q.device)
+    return dq, dk, dv
 
 
 def check_workspace(workspace: torch.Tensor) -> int:

@@ -19,6 +19,7 @@
  *                   dense + sparse rows of delta_decode_forward            delta_attention/llama.py:552-634
  *   dta_rows     <- qsa_kernel (attention for a list of query rows, row i
  *                   attending keys [0, limit_i])                 delta_attention/delta_kernel.py:259-329
+ *   dta_backward <- autograd of delta_forward_train               delta_attention/train/flex_delta.py:95-196
  */
 #ifndef DELTA_ATTENTION_B200_H
 #define DELTA_ATTENTION_B200_H
@@ -30,7 +31,7 @@
 extern "C" {
 #endif
 
-#define DTA_ABI_VERSION 2
+#define DTA_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define DTA_API __attribute__((visibility("default")))
@@ -110,6 +111,12 @@ typedef struct dta_prefill_args {
                              anchors, delta mode: dense - sparse of every anchor row, computed earlier
                              (the adaptive stride planner has it); the ROWS phase then computes only
                              the dense tail rows and WINDOW applies these rows */
+  float* lse_sparse;      /* optional out [batch, n_heads, seq_len] fp32: base-2 log-sum-exp of the scaled
+                             scores (log2 of the softmax denominator, scores times scaling * log2(e)) of
+                             each windowed row's sparse attention, rows [0, s_p) (every row in sparse-only
+                             mode; other rows untouched).  Kept by the training forward for dta_backward */
+  float* lse_dense;       /* optional out [batch, n_heads, n_sel] fp32: the same for each dense row of the
+                             ROWS phase, list order (anchors, then the tail rows s_p .. seq_len-1) */
 } dta_prefill_args;
 
 /* Test hook: the producer warp of every CTA first waits on a barrier that
@@ -211,10 +218,51 @@ DTA_API int dta_decode(const dta_decode_args* args, void* stream);
 #define DTA_DECODE_NOALLOC_SCRATCH_BYTES (32u << 20)
 DTA_API int dta_decode_noalloc(const dta_decode_args* args, void* stream);
 
+/* Training backward of one delta-attention layer with uniform anchors: the
+ * gradients of delta_forward_train (delta_attention/train/flex_delta.py:95-196,
+ * including its detach_delta / delta_grad_scale arms) with respect to q, k, v.
+ * Inputs are the forward's own q, k, v, its output and what a dta_prefill call
+ * with anchor_delta, lse_sparse and lse_dense set returned (same gamma, window,
+ * sink, q_block and scaling).
+ * grad_out: [batch, seq_len, n_heads, head_dim] bf16 contiguous (the output's layout).
+ * grad_q: [batch, n_heads, seq_len, head_dim]; grad_k, grad_v: [batch, n_kv_heads,
+ * seq_len, head_dim]; all bf16 contiguous.  n_heads / n_kv_heads must be 1, 2, 4 or 8.
+ * The workspace (dta_backward_workspace_size) holds the passes' output gradients,
+ * row sums and fp32 dK / dV accumulators; dta_check_workspace reads its error word. */
+typedef struct dta_backward_args {
+  int32_t abi_version;
+  int32_t batch, n_heads, n_kv_heads, seq_len, head_dim;
+  const void* q;
+  int64_t q_stride_b, q_stride_h, q_stride_s;
+  const void* k;
+  int64_t k_stride_b, k_stride_h, k_stride_s;
+  const void* v;
+  int64_t v_stride_b, v_stride_h, v_stride_s;
+  const void* out;          /* the forward's output */
+  const void* grad_out;
+  const float* anchor_delta; /* the forward's fp32 dense - sparse per anchor [batch, n_anchor, n_heads, head_dim] */
+  const float* lse_sparse;  /* the forward's lse_sparse [batch, n_heads, seq_len] */
+  const float* lse_dense;   /* the forward's lse_dense [batch, n_heads, n_sel] */
+  void* grad_q;
+  void* grad_k;
+  void* grad_v;
+  float scaling;
+  int32_t gamma, window, sink, q_block;
+  float delta_grad_scale;   /* factor on the gradient through the broadcast delta (the reference's
+                               delta_grad_scale); 0 = the detach_delta arm */
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t* error_word;      /* as in dta_prefill_args */
+  int64_t wait_cycles;      /* as in dta_prefill_args */
+} dta_backward_args;
+DTA_API size_t dta_backward_workspace_size(const dta_backward_args* args);
+DTA_API int dta_backward(const dta_backward_args* args, void* stream);
+
 /* Host-side helpers. */
 DTA_API int dta_abi_version(void);
 DTA_API const char* dta_status_string(int status);
-/* Last CUDA runtime error code seen by this thread (0 if none). */
+/* Last CUDA runtime error code seen by this thread (0 if none); for a failed TMA
+ * tensor-map encode, the driver's CUresult. */
 DTA_API int dta_last_cuda_error(void);
 /* Synchronously read the kernel error word of a workspace used on `stream`;
  * returns DTA_OK or DTA_ERR_KERNEL_TIMEOUT (kernel code in *kernel_code). */

@@ -24,6 +24,9 @@ Semantics restated here
   modes ``sparse-only`` (``:695-696``) and ``recompute`` (``:725-731``).
 * variable-stride correction: ``delta_attention/stride.py:26-40``.
 * decode: ``delta_attention/llama.py:498-634``.
+* training forward with autograd (the checker of the backward kernels):
+  ``delta_attention/train/flex_delta.py:95-196`` including its
+  ``detach_delta`` / ``delta_grad_scale`` arms (``_ScaleGrad``, ``:79-93``).
 """
 
 from __future__ import annotations
@@ -52,6 +55,7 @@ __all__ = [
     "delta_decode_step",
     "uniform_effective_sparsity",
     "row_cos",
+    "delta_forward_train",
 ]
 
 # hip-attn block_sparse_block_size_q; the window is anchored per block of this
@@ -386,3 +390,48 @@ def row_cos(a, b) -> torch.Tensor:
     a32 = a.reshape(a.size(0), a.size(1), -1).double()
     b32 = b.reshape(b.size(0), b.size(1), -1).double()
     return torch.nn.functional.cosine_similarity(a32, b32, dim=-1)
+
+
+# --------------------------------------------------------------------------
+# f4: differentiable training forward (checker of the backward kernels)
+# --------------------------------------------------------------------------
+
+class _ScaleGrad(torch.autograd.Function):
+    """Identity forward, gradient times a constant backward
+    (``delta_attention/train/flex_delta.py:79-93``)."""
+
+    @staticmethod
+    def forward(ctx, x, scale):
+        ctx.scale = scale
+        return x
+
+    @staticmethod
+    def backward(ctx, grad):
+        return grad * ctx.scale, None
+
+
+def delta_forward_train(q, k, v, gamma: int, window: int, sink: int = 1024, scaling: Optional[float] = None,
+                        detach_delta: bool = False, delta_grad_scale: float = 1.0, q_block: int = Q_BLOCK,
+                        dtype=torch.float64) -> torch.Tensor:
+    """The composition of ``delta_attention/train/flex_delta.py:95-196`` on this
+    module's differentiable primitives: sparse rows for every position, dense
+    rows for the anchors and the tail (``:176-186``), delta = dense[anchor] -
+    sparse[anchor] (``:188``), detached or gradient-scaled (``:189-192``), and
+    the broadcast (``:194-199``).  Autograd through it gives the reference
+    gradients for the backward kernels (q, k, v may require grad)."""
+    b, H, s, d = q.shape
+    if scaling is None:
+        scaling = d ** -0.5
+    _check_layout(s, gamma)
+    sparse = sparse_rows(q, k, v, torch.arange(s), window, sink, scaling, q_block, dtype)
+    anchors, tail, s_p = anchor_layout(s, gamma)
+    sel = torch.cat((anchors, tail))
+    dense = dense_rows(q, k, v, sel, scaling, dtype=dtype)
+    n = anchors.numel()
+    delta = dense[:, :n] - sparse[:, anchors]
+    if detach_delta:
+        delta = delta.detach()
+    elif delta_grad_scale != 1.0:
+        delta = _ScaleGrad.apply(delta, delta_grad_scale)
+    corrected = (sparse[:, :s_p].reshape(b, n, gamma, H, d) + delta.reshape(b, n, 1, H, d)).reshape(b, s_p, H, d)
+    return torch.cat((corrected, dense[:, n:]), dim=1)

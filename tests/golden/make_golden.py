@@ -229,6 +229,57 @@ def gen_decode(ref: str, out_dir: str) -> None:
     print("[golden] decode_reference", rec, flush=True)
 
 
+# name: (s, H, Hkv, d, gamma, window, sink, seed)
+TRAIN_FD_CASES = {
+    "train_small": (512, 4, 1, 64, 64, 128, 32, 0),
+    "train_gqa2_g32": (768, 4, 2, 64, 32, 256, 64, 1),
+    "train_d128_g128": (1024, 8, 2, 128, 128, 192, 128, 2),
+}
+TRAIN_FD_DIRS = 3
+TRAIN_FD_EPS = 1e-5
+
+
+def train_fd_tensors(case, dir_index: int):
+    """Inputs (float64 of the bf16-rounded synthetic q/k/v), the loss weights W
+    and direction ``dir_index`` of a finite-difference case; shared with the
+    test that checks the oracle's gradients against the stored values."""
+    s, H, Hkv, d, gamma, window, sink, seed = case
+    q, k, v = make_inputs(s, H, Hkv, d, seed=seed, rope_theta=500000.0, dtype=torch.bfloat16)
+    q, k, v = q.double(), k.double(), v.double()
+    g = torch.Generator().manual_seed(9000 + seed)
+    w = torch.randn(1, s, H, d, generator=g, dtype=torch.float64)
+    g = torch.Generator().manual_seed(9100 + 10 * seed + dir_index)
+    dirs = tuple(torch.randn(t.shape, generator=g, dtype=torch.float64) for t in (q, k, v))
+    return (q, k, v), w, dirs
+
+
+def gen_train_fd(ref: str, out_dir: str) -> None:
+    """Directional derivatives of L = sum(W * out) of the reference's own
+    ``delta_forward_train`` (eager FlexAttention has no CPU backward, so central
+    finite differences of its float64 forward along seeded random directions of
+    (q, k, v) jointly stand in for its gradients)."""
+    flex_delta = load_flex(ref)
+    torch.set_num_threads(os.cpu_count() or 1)
+    rec = {"eps": TRAIN_FD_EPS, "cases": {}}
+    for name, case in TRAIN_FD_CASES.items():
+        s, H, Hkv, d, gamma, window, sink, seed = case
+        vals = []
+        for i in range(TRAIN_FD_DIRS):
+            (q, k, v), w, (dq, dk, dv) = train_fd_tensors(case, i)
+
+            def loss(e):
+                with torch.no_grad():
+                    o = flex_delta.delta_forward_train(q + e * dq, k + e * dk, v + e * dv, gamma=gamma,
+                                                       window=window, sink=sink)
+                return float((o.double() * w).sum())
+
+            vals.append((loss(TRAIN_FD_EPS) - loss(-TRAIN_FD_EPS)) / (2 * TRAIN_FD_EPS))
+        rec["cases"][name] = {"case": list(case), "directional_derivatives": vals}
+        print(f"[golden] train_fd {name}: {vals}", flush=True)
+    with open(os.path.join(out_dir, "train_fd.json"), "w") as f:
+        json.dump(rec, f, indent=1)
+
+
 def gen_cpu_timing(ref: str, out_dir: str, repeats: int = 2) -> None:
     """Time the reference's own CPU path (``delta_forward_train``, eager
     FlexAttention, fp32) against this repository's CPU oracle port on the same
@@ -285,6 +336,8 @@ def main() -> None:
     ap.add_argument("--only", nargs="*")
     ap.add_argument("--timing-only", action="store_true",
                     help="only write cpu_timing.json (reference CPU path vs the oracle port)")
+    ap.add_argument("--train-fd-only", action="store_true",
+                    help="only write train_fd.json (finite differences of the reference's training forward)")
     args = ap.parse_args()
     if not args.reference:
         raise SystemExit("pass --reference <checkout> or set DTA_REFERENCE")
@@ -293,9 +346,13 @@ def main() -> None:
     if args.timing_only:
         gen_cpu_timing(args.reference, HERE)
         return
+    if args.train_fd_only:
+        gen_train_fd(args.reference, HERE)
+        return
     gen_stride(args.reference, HERE)
     gen_decode(args.reference, HERE)
     gen_flex(args.reference, HERE, args.only)
+    gen_train_fd(args.reference, HERE)
 
 
 if __name__ == "__main__":

@@ -93,3 +93,45 @@ def test_oracle_decode_matches_reference(golden_dir):
             assert (out - ref[t].double()).abs().max().item() < 2e-5, (policy, t)
     sp = orc.sparse_decode(qs[0], k, v, meta["window"], meta["sink"], sc)
     assert (sp - torch.from_numpy(z["out_sparse"]).double()).abs().max().item() < 2e-5
+
+
+def test_oracle_gradients_match_reference_finite_differences(golden_dir):
+    """The oracle's training forward, differentiated by autograd, against central
+    finite differences of the reference's own ``delta_forward_train`` along the
+    same seeded directions (``tests/golden/train_fd.json``)."""
+    from tests.golden.make_golden import TRAIN_FD_CASES, train_fd_tensors
+
+    with open(os.path.join(golden_dir, "train_fd.json")) as f:
+        rec = json.load(f)
+    for name, case in TRAIN_FD_CASES.items():
+        want = rec["cases"][name]["directional_derivatives"]
+        assert rec["cases"][name]["case"] == list(case)
+        s, H, Hkv, d, gamma, window, sink, seed = case
+        for i, fd in enumerate(want):
+            (q, k, v), w, dirs = train_fd_tensors(case, i)
+            q, k, v = (t.clone().requires_grad_(True) for t in (q, k, v))
+            out = orc.delta_forward_train(q, k, v, gamma, window, sink)
+            (out * w).sum().backward()
+            got = sum(float((t.grad * dt).sum()) for t, dt in zip((q, k, v), dirs))
+            assert abs(got - fd) <= 1e-6 * max(1.0, abs(fd)), f"{name} dir {i}: autograd {got} vs reference fd {fd}"
+
+
+def test_oracle_training_arms():
+    """detach_delta keeps the forward and removes the delta path's gradient;
+    delta_grad_scale interpolates (flex_delta.py:189-192)."""
+    torch.manual_seed(3)
+    s, H, Hkv, d = 512, 4, 1, 32
+    q0, k0, v0 = (torch.randn(1, h, s, d, dtype=torch.float64) for h in (H, Hkv, Hkv))
+    w = torch.randn(1, s, H, d, dtype=torch.float64)
+
+    def grads(**kw):
+        q, k, v = (t.clone().requires_grad_(True) for t in (q0, k0, v0))
+        out = orc.delta_forward_train(q, k, v, 64, 128, 32, **kw)
+        (out * w).sum().backward()
+        return out.detach(), q.grad, k.grad, v.grad
+
+    full, det, half = grads(), grads(detach_delta=True), grads(delta_grad_scale=0.5)
+    assert torch.equal(full[0], det[0]) and torch.equal(full[0], half[0])
+    for a, b, c in zip(full[1:], det[1:], half[1:]):
+        assert (a - b).norm() > 1e-3 * a.norm()
+        assert torch.allclose(c, 0.5 * (a + b), atol=1e-10)
