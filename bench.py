@@ -68,8 +68,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-clocks", action="store_true")
-    ap.add_argument("--op", choices=["prefill", "decode"], default="prefill",
-                    help="decode: HBM throughput of the dense / sparse / one-pass decode kernels")
+    ap.add_argument("--op", choices=["prefill", "decode", "train"], default="prefill",
+                    help="decode: HBM throughput of the dense / sparse / one-pass decode kernels; "
+                         "train: forward + backward of one layer")
     ap.add_argument("--decode-caches", type=int, default=8,
                     help="distinct KV caches cycled through per decode replay (defeats L2 reuse)")
     return ap.parse_args()
@@ -375,6 +376,82 @@ def run_decode(args, local_rank):
 
 
 # ---------------------------------------------------------------------------
+# training step of one layer (bench.py --op train)
+# ---------------------------------------------------------------------------
+def run_train(args, local_rank):
+    """Forward + backward of one delta-attention layer through the autograd
+    drop-in (``delta_attention_b200.train.delta_forward_train``), the
+    reference's per-layer training measurement (Llama-8B dims, gamma 64, sink
+    1024 + window 2048 when run with ``--sink 1024``; docs/STATS.md:302-318).
+    Roofline: analytic training FLOPs = 3.5 x the forward's north_star count
+    (forward 2 products per attended pair, backward 5), over the CUDA-event
+    time of a step; the forward and the backward are also timed alone."""
+    import torch
+
+    from delta_attention_b200 import train
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    H, Hkv, d, n = args.heads, args.kv_heads, args.head_dim, args.seq
+    gen = torch.Generator(device=dev).manual_seed(0)
+    q = (torch.randn(1, H, n, d, generator=gen, device=dev) * 0.5).bfloat16().requires_grad_(True)
+    k = (torch.randn(1, Hkv, n, d, generator=gen, device=dev) * 0.5).bfloat16().requires_grad_(True)
+    v = (torch.randn(1, Hkv, n, d, generator=gen, device=dev) * 0.5).bfloat16().requires_grad_(True)
+    g = torch.randn(1, n, H, d, generator=gen, device=dev).bfloat16()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    peaks, peaks_src = load_peaks()
+    fwd_flops = analytic_flops(H, d, n, args.window, args.sink, args.gamma)[0]
+    flops = 3.5 * fwd_flops
+
+    def step():
+        out = train.delta_forward_train(q, k, v, args.gamma, args.window, args.sink)
+        out.backward(g)
+        return out
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    times, t_fwd, t_bwd = [], [], []
+    sampler = ClockSampler(physical_gpu(local_rank), enabled=not args.no_clocks)
+    with sampler:
+        for _ in range(max(1, args.steps)):
+            flush.zero_()
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            e[0].record()
+            out = train.delta_forward_train(q, k, v, args.gamma, args.window, args.sink)
+            e[1].record()
+            out.backward(g)
+            e[2].record()
+            e[2].synchronize()
+            t_fwd.append(e[0].elapsed_time(e[1]))
+            t_bwd.append(e[1].elapsed_time(e[2]))
+            times.append(e[0].elapsed_time(e[2]))
+    ms = statistics.median(times)
+    achieved = flops / (ms * 1e-3) / 1e12
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    G = H // Hkv
+    fused = G in (4, 8) and args.gamma >= 8 and args.gamma & (args.gamma - 1) == 0
+    line = {
+        "metric": "delta-attn training step (forward + backward) of one layer, tokens/s", "op": "train",
+        "value": n / (ms * 1e-3), "unit": "tokens/s", "higher_is_better": True, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "dtype": "bf16", "data": "synthetic (seeded N(0,1)*0.5 q/k/v)",
+        "config": {"workload": "single-layer delta-attention forward + backward (reference training protocol)",
+                   "seq_len": n, "n_heads": H, "n_kv_heads": Hkv, "head_dim": d, "window": args.window,
+                   "sink": args.sink, "gamma": args.gamma, "l2": "256 MB flush before every step"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": peaks_src, "flops_per_step": flops,
+                     "flops_note": "3.5 x 4*H*d*(N*(W+S) + (N/gamma)*N/2)"},
+        "phases_ms": {"forward": statistics.median(t_fwd), "backward": statistics.median(t_bwd)},
+        # forward: rows + windowed launches (+ the delta kernel when not fused);
+        # backward: prep, plan, key-major, two query-major, finalize
+        "gpu_launches": ((2 if fused else 3) + 6) * args.steps,
+        "clocks": sampler.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
 def run_b200(args, rank, world, local_rank):
@@ -601,6 +678,11 @@ def main():
             print(json.dumps({"error": "--op decode runs on one GPU"}), flush=True)
             return 2
         return run_decode(args, local_rank)
+    if args.op == "train":
+        if world > 1:
+            print(json.dumps({"error": "--op train runs on one GPU"}), flush=True)
+            return 2
+        return run_train(args, local_rank)
     if world > 1:
         import datetime
 
