@@ -196,24 +196,52 @@ cudaError_t launch_backward_prep(const __nv_bfloat16* q, long long q_sb, long lo
   return cudaGetLastError();
 }
 
-// chunk_base[kt] = first chunk of key tile kt in the key-major launch
-__global__ void backward_plan_kernel(int* chunk_base, int n_ktiles, int S, int s_p, int n_anchor, int n_sel, int gamma,
-                                     int window, int sink, int qblock, int R, int chunk_iters) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  int acc = 0;
-  for (int kt = 0; kt < n_ktiles; ++kt) {
-    chunk_base[kt] = acc;
+// chunk_base[kt] = first chunk of key tile kt in the key-major launch: each of
+// the 1024 threads counts the chunks of a run of consecutive key tiles, then a
+// block-wide exclusive scan (warp shuffles, then the 32 warp totals) places them
+constexpr int PLAN_THREADS = 1024;
+
+__global__ void __launch_bounds__(PLAN_THREADS) backward_plan_kernel(int* chunk_base, int n_ktiles, int S, int s_p,
+                                                                     int n_anchor, int n_sel, int gamma, int window,
+                                                                     int sink, int qblock, int R, int chunk_iters) {
+  __shared__ int warp_tot[PLAN_THREADS / 32];
+  const int per = (n_ktiles + PLAN_THREADS - 1) / PLAN_THREADS;
+  const int t0 = threadIdx.x * per, t1 = min(t0 + per, n_ktiles);
+  auto chunks = [&](int kt) {
     const KeyTileList L = bwd_key_tile_list(kt, S, s_p, n_anchor, n_sel, gamma, window, sink, qblock, R);
-    const int n = (L.us1 - L.us0) + (L.ud1 - L.ud0);
-    acc += (n + chunk_iters - 1) / chunk_iters;
+    return ((L.us1 - L.us0) + (L.ud1 - L.ud0) + chunk_iters - 1) / chunk_iters;
+  };
+  int mine = 0;
+  for (int kt = t0; kt < t1; ++kt) mine += chunks(kt);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = mine;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
   }
-  chunk_base[n_ktiles] = acc;
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_tot[lane];
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    warp_tot[lane] = w;  // inclusive over warps
+  }
+  __syncthreads();
+  int acc = (warp > 0 ? warp_tot[warp - 1] : 0) + incl - mine;  // exclusive prefix of this thread's run
+  for (int kt = t0; kt < t1; ++kt) {
+    chunk_base[kt] = acc;
+    acc += chunks(kt);
+  }
+  if (threadIdx.x == PLAN_THREADS - 1) chunk_base[n_ktiles] = warp_tot[31];
 }
 
 cudaError_t launch_backward_plan(int* chunk_base, int n_ktiles, int S, int s_p, int n_anchor, int n_sel, int gamma,
                                  int window, int sink, int qblock, int R, int chunk_iters, cudaStream_t stream) {
-  backward_plan_kernel<<<1, 32, 0, stream>>>(chunk_base, n_ktiles, S, s_p, n_anchor, n_sel, gamma, window, sink, qblock,
-                                             R, chunk_iters);
+  backward_plan_kernel<<<1, PLAN_THREADS, 0, stream>>>(chunk_base, n_ktiles, S, s_p, n_anchor, n_sel, gamma, window,
+                                                       sink, qblock, R, chunk_iters);
   return cudaGetLastError();
 }
 
@@ -271,9 +299,16 @@ struct BGeo {
   static constexpr int FIX_OFF = BWD_CTRL;
   static constexpr int STR_OFF = FIX_OFF + 2 * TILE;
   static constexpr int SMEM = STR_OFF + NST * STAGE + 1024;  // + alignment slack
+  // query-major: separate rings, K for three iterations (read by S and by dQ),
+  // V for two (read by dP only, released as soon as dP is done)
+  static constexpr int KST = 3, VST = 2;
+  static constexpr int K_OFF = FIX_OFF + 2 * TILE;
+  static constexpr int V_OFF = K_OFF + KST * TILE;
+  static constexpr int SMEM_QM = V_OFF + VST * TILE + 1024;
   static constexpr int T1 = 0, T2 = 128, ACC1 = 256, ACC2 = 256 + HD;
+  static constexpr int DS = 384;  // query-major: two bf16 dS buffers of 64 columns
 };
-static_assert(BGeo<128>::SMEM <= 232448, "shared memory budget");
+static_assert(BGeo<128>::SMEM <= 232448 && BGeo<128>::SMEM_QM <= 232448, "shared memory budget");
 static_assert(BGeo<128>::STAGE % 1024 == 0 && BGeo<64>::STAGE % 1024 == 0, "tiles stay 1024-byte aligned");
 
 struct BCtrl {
@@ -281,6 +316,9 @@ struct BCtrl {
   uint64_t fix_full, fix_empty;
   uint64_t st_full[2], st_empty[2];
   uint64_t s_full, p_full, acc_full, acc_empty;
+  uint64_t k_full[3], k_empty[3], v_full[2], v_empty[2];  // query-major rings
+  uint64_t s_free;      // query-major: S and dP of the iteration are in registers
+  uint64_t ds_free[2];  // query-major: the dQ product has read dS buffer b
   uint64_t drain;
   // job record: [0] kind (1 job, -1 end), [1] b, [2] g, [3] tile, [4] i0,
   // [5] i1, [6] n0, [7] w0, [8] us0, [9] us1, [10] ud0
@@ -406,6 +444,17 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
     mbar_init(BBAR(p_full), 8);
     mbar_init(BBAR(acc_full), 1);
     mbar_init(BBAR(acc_empty), 8);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(BBAR(k_full[0]) + 8 * i, 1);
+      mbar_init(BBAR(k_empty[0]) + 8 * i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(BBAR(v_full[0]) + 8 * i, 1);
+      mbar_init(BBAR(v_empty[0]) + 8 * i, 1);
+    }
+    mbar_init(BBAR(s_free), 8);
+    mbar_init(BBAR(ds_free[0]), 1);
+    mbar_init(BBAR(ds_free[0]) + 8, 1);
     mbar_init(BBAR(drain), 1);
     ctrl->abort_flag = 0;
     mbar_init_fence();
@@ -435,6 +484,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
   if (warp == 0) {
     // ======================= producer =======================
     int n = 0;            // stream items issued (stage ring position)
+    int nk = 0, nv = 0;   // query-major: K / V loads issued (for the drain on abort)
     int jobs = 0;         // jobs whose fixed tiles were loaded
     bool ok = true;
     for (int it = 0; ok; ++it) {
@@ -476,7 +526,36 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
           }
         }
       }
-      // the streamed operand pair of every iteration
+      if constexpr (!KM) {
+        // query-major: K and V of every key tile through their rings
+        for (int u = J.i0; u < J.i1; ++u, ++n) {
+          const int kt = u < J.n0 ? u : J.w0 + (u - J.n0);
+          const int ks = n % G::KST, vs = n % G::VST;
+          if (!mbar_wait_warp(BBAR(k_empty[0]) + 8 * ks, ((n / G::KST) & 1) ^ 1, wc, KERR_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            const uint32_t kd = base_u32 + G::K_OFF + ks * G::TILE;
+            mbar_arrive_expect_tx(BBAR(k_full[0]) + 8 * ks, G::TILE);
+            for (int rg = 0; rg < G::REGIONS; ++rg)
+              tma_load_4d(kd + rg * G::REGION, &p.tm_k, BBAR(k_full[0]) + 8 * ks, rg * 64, kt * BWD_BN, J.g, J.b);
+          }
+          nk = n + 1;
+          if (!mbar_wait_warp(BBAR(v_empty[0]) + 8 * vs, ((n / G::VST) & 1) ^ 1, wc, KERR_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            const uint32_t vd = base_u32 + G::V_OFF + vs * G::TILE;
+            mbar_arrive_expect_tx(BBAR(v_full[0]) + 8 * vs, G::TILE);
+            for (int rg = 0; rg < G::REGIONS; ++rg)
+              tma_load_4d(vd + rg * G::REGION, &p.tm_v, BBAR(v_full[0]) + 8 * vs, rg * 64, kt * BWD_BN, J.g, J.b);
+          }
+          nv = n + 1;
+        }
+      } else {
+      // key-major: the streamed operand pair (q, dO tiles and their rows' lse, D)
       for (int u = J.i0; u < J.i1; ++u, ++n) {
         const int st = n & 1;
         if (!mbar_wait_warp(BBAR(st_empty[0]) + 8 * st, ((n >> 1) & 1) ^ 1, wc, KERR_TIMEOUT_PRODUCER)) {
@@ -523,16 +602,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
               }
             }
           }
-        } else {
-          const int kt = u < J.n0 ? u : J.w0 + (u - J.n0);
-          if (lane == 0) {
-            mbar_arrive_expect_tx(BBAR(st_full[0]) + 8 * st, 2 * G::TILE);
-            for (int rg = 0; rg < G::REGIONS; ++rg) {
-              tma_load_4d(s0 + rg * G::REGION, &p.tm_k, BBAR(st_full[0]) + 8 * st, rg * 64, kt * BWD_BN, J.g, J.b);
-              tma_load_4d(s1 + rg * G::REGION, &p.tm_v, BBAR(st_full[0]) + 8 * st, rg * 64, kt * BWD_BN, J.g, J.b);
-            }
-          }
         }
+      }
       }
     }
     // on abort, loads in flight land before the CTA can exit: the last stage
@@ -543,7 +614,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
         while (!mbar_try_wait(bar, parity))
           if (clock64() - t0 > kWaitTimeoutCycles) break;
       };
-      for (int m = max(0, n - G::NST); m < n; ++m) drain(BBAR(st_full[0]) + 8 * (m & 1), (uint32_t)((m >> 1) & 1));
+      if constexpr (KM) {
+        for (int m = max(0, n - G::NST); m < n; ++m) drain(BBAR(st_full[0]) + 8 * (m & 1), (uint32_t)((m >> 1) & 1));
+      } else {
+        for (int m = max(0, nk - G::KST); m < nk; ++m)
+          drain(BBAR(k_full[0]) + 8 * (m % G::KST), (uint32_t)((m / G::KST) & 1));
+        for (int m = max(0, nv - G::VST); m < nv; ++m)
+          drain(BBAR(v_full[0]) + 8 * (m % G::VST), (uint32_t)((m / G::VST) & 1));
+      }
       if (jobs > 0) drain(BBAR(fix_full), (uint32_t)((jobs - 1) & 1));
     }
   } else if (warp == 1) {
@@ -567,6 +645,77 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
       if (lane == 0) mbar_arrive(BBAR(job_empty[0]) + 8 * slot);
       if (end) break;
       if (!mbar_poll(BBAR(fix_full), jobs & 1, wc, KERR_TIMEOUT_MMA)) break;
+      if constexpr (!KM) {
+        // Query-major, pipelined: S and dP of iteration m + 1 are issued as
+        // soon as the compute warpgroups hold iteration m's in registers
+        // (s_free), before dQ(m); dS(m) lives in its own TMEM buffer
+        // (DS + 64 (m & 1)), so dQ(m) and S(m + 1) do not share columns.
+        auto issue_ss = [&](int m) -> bool {
+          const int ks = m % G::KST, vs = m % G::VST;
+          if (!mbar_poll(BBAR(k_full[0]) + 8 * ks, (m / G::KST) & 1, wc, KERR_TIMEOUT_MMA)) return false;
+          if (!mbar_poll(BBAR(v_full[0]) + 8 * vs, (m / G::VST) & 1, wc, KERR_TIMEOUT_MMA)) return false;
+          if (m > 0 && !mbar_poll(BBAR(s_free), (m - 1) & 1, wc, KERR_TIMEOUT_MMA)) return false;
+          tc_fence_after();
+          const uint32_t s0 = base_u32 + G::K_OFF + ks * G::TILE, s1 = base_u32 + G::V_OFF + vs * G::TILE;
+          const uint64_t sdesc0 = smem_desc_sw128(s0, 16, 1024), sdesc1 = smem_desc_sw128(s1, 16, 1024);
+          if (elect_one()) {
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; ++kk) {
+              const uint32_t off = ((kk >> 2) * G::REGION + (kk & 3) * 32) >> 4;
+              umma_ss(tmem + G::T1, fdesc0 + off, sdesc0 + off, IDESC_SS, kk > 0 ? 1u : 0u);
+            }
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; ++kk) {
+              const uint32_t off = ((kk >> 2) * G::REGION + (kk & 3) * 32) >> 4;
+              umma_ss(tmem + G::T2, fdesc1 + off, sdesc1 + off, IDESC_SS, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(BBAR(s_full));
+            umma_commit(BBAR(v_empty[0]) + 8 * vs);  // V is read by dP only
+          }
+          __syncwarp();
+          return true;
+        };
+        auto issue_ts = [&](int m, bool first, bool last) -> bool {
+          const int ks = m % G::KST;
+          if (!mbar_poll(BBAR(p_full), m & 1, wc, KERR_TIMEOUT_MMA)) return false;
+          if (first && jobs > 0 && !mbar_poll(BBAR(acc_empty), (jobs - 1) & 1, wc, KERR_TIMEOUT_MMA)) return false;
+          tc_fence_after();
+          const uint64_t mdesc0 = smem_desc_sw128(base_u32 + G::K_OFF + ks * G::TILE, G::REGION, 1024);
+          const uint32_t ds = tmem + G::DS + (uint32_t)(m & 1) * 64;
+          if (elect_one()) {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_ts(tmem + G::ACC1, ds + kk * 8, mdesc0 + ((kk * 2048) >> 4), IDESC_TS, (!first || kk > 0) ? 1u : 0u);
+            umma_commit(BBAR(k_empty[0]) + 8 * ks);
+            umma_commit(BBAR(ds_free[0]) + 8 * (m & 1));
+            if (last) umma_commit(BBAR(acc_full));
+          }
+          __syncwarp();
+          return true;
+        };
+        const int T = i1 - i0;
+        if (!issue_ss(n)) break;
+        for (int k = 0; k < T; ++k) {
+          if (k + 1 < T) {
+            if (!issue_ss(n + k + 1)) {
+              aborted = true;
+              break;
+            }
+          } else {
+            // the job's fixed tiles are read by its S / dP products only
+            if (elect_one()) umma_commit(BBAR(fix_empty));
+            __syncwarp();
+          }
+          if (!issue_ts(n + k, k == 0, k == T - 1)) {
+            aborted = true;
+            break;
+          }
+        }
+        if (aborted) break;
+        n += T;
+        ++jobs;
+      } else {
+      // key-major: S^T, dP^T, then dV and dK from P^T / dS^T written over them
       for (int u = i0; u < i1; ++u, ++n) {
         const int st = n & 1;
         if (!mbar_poll(BBAR(st_full[0]) + 8 * st, (n >> 1) & 1, wc, KERR_TIMEOUT_MMA)) {
@@ -608,12 +757,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t acol = kk < 4 ? kk * 8 : 64 + (kk - 4) * 8;
             const uint32_t acc = (u > i0 || kk > 0) ? 1u : 0u;
-            if constexpr (KM) {
-              umma_ts(tmem + G::ACC1, tmem + G::T1 + acol, mdesc1 + ((kk * 2048) >> 4), IDESC_TS, acc);  // dV += P^T dO
-              umma_ts(tmem + G::ACC2, tmem + G::T2 + acol, mdesc0 + ((kk * 2048) >> 4), IDESC_TS, acc);  // dK += dS^T Q
-            } else {
-              umma_ts(tmem + G::ACC1, tmem + G::T1 + acol, mdesc0 + ((kk * 2048) >> 4), IDESC_TS, acc);  // dQ += dS K
-            }
+            umma_ts(tmem + G::ACC1, tmem + G::T1 + acol, mdesc1 + ((kk * 2048) >> 4), IDESC_TS, acc);  // dV += P^T dO
+            umma_ts(tmem + G::ACC2, tmem + G::T2 + acol, mdesc0 + ((kk * 2048) >> 4), IDESC_TS, acc);  // dK += dS^T Q
           }
           umma_commit(BBAR(st_empty[0]) + 8 * st);
           if (u == i1 - 1) umma_commit(BBAR(acc_full));
@@ -622,6 +767,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
       }
       if (aborted) break;
       ++jobs;
+      }
     }
     __syncwarp();
     if (elect_one()) umma_commit(BBAR(drain));
@@ -695,6 +841,54 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
         }
       }
       bool aborted = false;
+      if constexpr (!KM) {
+        // query-major: take S and dP of the iteration into registers and
+        // release them at once (the MMA issuer starts the next iteration's S
+        // and dP), then form dS into this iteration's dS buffer
+        for (int u = J.i0; u < J.i1; ++u, ++n) {
+          if (!mbar_wait_warp(BBAR(s_full), n & 1, wc, KERR_TIMEOUT_SOFTMAX)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const int kt = u < J.n0 ? u : J.w0 + (u - J.n0);
+          // 32 columns at a time; S and dP are released once the second
+          // chunk is in registers (the first chunk's dS is formed meanwhile)
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float sv[32], dv[32];
+            tmem_ld32f(tmem + lane_off + G::T1 + wg * 64 + c * 32, sv);
+            tmem_ld32f(tmem + lane_off + G::T2 + wg * 64 + c * 32, dv);
+            tmem_wait_ld();
+            if (c == 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(BBAR(s_free));
+            }
+            const int kb = kt * BWD_BN + wg * 64 + c * 32;
+            uint32_t m = qvalid ? bits_range(0, qpos - kb + 1) : 0u;
+            if (p.pass == BWD_SPARSE) m &= bits_range(0, p.sink - kb) | bits_range(qlo - kb, 32);
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float p0 = ((m >> e) & 1u) ? fast_exp2(sv[e] * sl2 - qlse) : 0.f;
+              const float p1 = ((m >> (e + 1)) & 1u) ? fast_exp2(sv[e + 1] * sl2 - qlse) : 0.f;
+              pk[c * 16 + (e >> 1)] = pack_bf16x2(p0 * (dv[e] - qd), p1 * (dv[e + 1] - qd));
+            }
+          }
+          // the dQ product two iterations back has read this dS buffer
+          if (!mbar_wait_warp(BBAR(ds_free[0]) + 8 * (n & 1), ((n >> 1) & 1) ^ 1, wc, KERR_TIMEOUT_SOFTMAX)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          tmem_st32(tmem + lane_off + G::DS + (n & 1) * 64 + wg * 32, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(BBAR(p_full));
+        }
+      } else
       for (int u = J.i0; u < J.i1; ++u, ++n) {
         if (!mbar_wait_warp(BBAR(s_full), n & 1, wc, KERR_TIMEOUT_SOFTMAX)) {
           aborted = true;
@@ -855,7 +1049,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
 
 template <int HD, int KIND>
 static cudaError_t launch_bwd_hd(const BackwardParams& p, int grid, cudaStream_t stream) {
-  const int smem = BGeo<HD>::SMEM;
+  const int smem = KIND == BWD_KM ? BGeo<HD>::SMEM : BGeo<HD>::SMEM_QM;
   cudaError_t e = cudaFuncSetAttribute(bwd_kernel<HD, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   bwd_kernel<HD, KIND><<<grid, BWD_THREADS, smem, stream>>>(p);
