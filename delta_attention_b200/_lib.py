@@ -120,6 +120,7 @@ class DecodeArgs(ctypes.Structure):
         ("window", c_i32), ("sink", c_i32),
         ("dense_out", c_vp), ("sparse_out", c_vp),
         ("workspace", c_vp), ("workspace_bytes", ctypes.c_size_t),
+        ("n_keys_dev", c_vp),
     ]
 
 

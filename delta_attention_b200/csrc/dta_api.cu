@@ -552,6 +552,14 @@ static void decode_chunking(const dta_decode_args* a, int C, bool sparse, bool a
   S->first_window_chunk = fw;
   if (!sparse || all_sparse) S->n_launched = S->n_chunks;
   else S->n_launched = S->n_sink_chunks + (S->n_chunks - fw);
+  if (sparse && a->n_keys_dev) {
+    // device key count: the window's chunks are placed on the device, so launch
+    // enough for any count up to the capacity (the sink chunks, then the window
+    // span plus one chunk of misalignment; with every key sparse the same
+    // number covers [0, sink + window))
+    const int span = S->n_sink_chunks + (a->window + C - 1) / C + 1;
+    S->n_launched = span < S->n_chunks ? span : S->n_chunks;
+  }
   S->partials = nullptr;
 }
 
@@ -579,7 +587,9 @@ static int decode_setup(const dta_decode_args* a, dta::DecodeParams* p, int sms)
   p->n_keys = n;
   p->scale_log2 = a->scaling * 1.4426950408889634f;
   p->window = a->window; p->sink = a->sink;
-  p->all_sparse = (n <= a->sink + a->window) ? 1 : 0;
+  p->n_keys_dev = a->n_keys_dev;
+  // with a device key count the kernels decide this per call
+  p->all_sparse = (!a->n_keys_dev && n <= a->sink + a->window) ? 1 : 0;
   decode_chunking(a, decode_dense_chunk(a, sms), false, p->all_sparse != 0, &p->set[0]);
   decode_chunking(a, dta::DEC_SPARSE_CHUNK, true, p->all_sparse != 0, &p->set[1]);
   return DTA_OK;
@@ -603,6 +613,7 @@ int dta_decode(const dta_decode_args* a, void* stream_) {
   int st = decode_setup(a, &p, 0);
   if (st != DTA_OK) return st;
   if (!a->q || !a->k || !a->v || (!a->dense_out && !a->sparse_out)) return DTA_ERR_INVALID_ARG;
+  if (a->n_keys_dev && ((uintptr_t)a->n_keys_dev & 3u) != 0) return DTA_ERR_ALIGNMENT;
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v)) return DTA_ERR_ALIGNMENT;
   if ((a->dense_out && !aligned16(a->dense_out)) || (a->sparse_out && !aligned16(a->sparse_out)))
     return DTA_ERR_ALIGNMENT;

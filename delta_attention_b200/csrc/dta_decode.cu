@@ -21,13 +21,25 @@ namespace dta {
 
 constexpr int DEC_THREADS = 128;
 
-__device__ __forceinline__ bool dec_sparse_key(const DecodeParams& p, int j) {
-  return p.all_sparse || j < p.sink || j >= p.n_keys - p.window;
+// the live key count and whether every key is sparse (host values, or read
+// from the device count for CUDA-graph replays)
+__device__ __forceinline__ int dec_n_keys(const DecodeParams& p) {
+  return p.n_keys_dev ? min(max(*p.n_keys_dev, 1), p.n_keys) : p.n_keys;
+}
+__device__ __forceinline__ bool dec_all_sparse(const DecodeParams& p, int n) {
+  return p.n_keys_dev ? n <= p.sink + p.window : p.all_sparse != 0;
 }
 
-__device__ __forceinline__ int dec_chunk_of_block(const DecodeParams& p, const DecodeSet& S, int x) {
-  if (!S.sparse || p.all_sparse) return x;
-  return x < S.n_sink_chunks ? x : S.first_window_chunk + (x - S.n_sink_chunks);
+__device__ __forceinline__ bool dec_sparse_key(const DecodeParams& p, bool all_sparse, int n, int j) {
+  return all_sparse || j < p.sink || j >= n - p.window;
+}
+
+__device__ __forceinline__ int dec_chunk_of_block(const DecodeParams& p, const DecodeSet& S, bool all_sparse, int n,
+                                                  int x) {
+  if (!S.sparse || all_sparse) return x;
+  // window chunks start at the chunk holding key n - window, after the sink chunks
+  const int fwc = p.n_keys_dev ? max(S.n_sink_chunks, max(n - p.window, 0) / S.chunk) : S.first_window_chunk;
+  return x < S.n_sink_chunks ? x : fwc + (x - S.n_sink_chunks);
 }
 
 
@@ -84,13 +96,15 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_mma_kernel(const __grid_co
   const uint32_t sbase = smem_u32(dsm);
 
   const DecodeSet& S = p.set[which];
-  const int c = dec_chunk_of_block(p, S, blockIdx.x);
+  const int n_live = dec_n_keys(p);
+  const bool all_sparse = dec_all_sparse(p, n_live);
+  const int c = dec_chunk_of_block(p, S, all_sparse, n_live, blockIdx.x);
   const int bg = blockIdx.y;
   const int b = bg / p.Hkv, g = bg - (bg / p.Hkv) * p.Hkv;
   const int G = p.G;
   const int k0 = c * S.chunk;
-  const int k1 = min(k0 + S.chunk, p.n_keys);
-  const int nk = k1 - k0;
+  const int k1 = min(k0 + S.chunk, n_live);
+  const int nk = max(k1 - k0, 0);  // 0: a chunk past the live keys (device count) leaves an empty partial
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gr = lane >> 2, cq = lane & 3;  // fragment row (= head) and column pair
   float* part0 = S.partials + ((long long)(b * p.H + g * G) * S.n_launched + blockIdx.x) * (4 + HD);
@@ -166,7 +180,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_mma_kernel(const __grid_co
     const int jk[4] = {jb + 2 * cq, jb + 2 * cq + 1, jb + 8 + 2 * cq, jb + 9 + 2 * cq};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const bool v = jk[e] < nk && (!S.sparse || dec_sparse_key(p, k0 + jk[e]));
+      const bool v = jk[e] < nk && (!S.sparse || dec_sparse_key(p, all_sparse, n_live, k0 + jk[e]));
       sv[e] = v ? sv[e] : -INFINITY;
     }
     float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
@@ -252,8 +266,9 @@ __global__ void decode_merge_kernel(const __grid_constant__ DecodeParams p) {
     __nv_bfloat16* dst = out == 0 ? p.dense_out : p.sparse_out;
     if (!dst) continue;
     // with n <= sink + window the two key sets coincide: both outputs come
-    // from the sparse set's partials
-    const DecodeSet& S = p.set[(out == 1 || p.all_sparse) ? 1 : 0];
+    // from the sparse set's partials (host key count; with a device count the
+    // dense output keeps the dense set, which covers the same keys)
+    const DecodeSet& S = p.set[(out == 1 || (!p.n_keys_dev && p.all_sparse)) ? 1 : 0];
     const float* base = S.partials + (long long)bh * S.n_launched * (4 + HD);
     float M = -INFINITY;
     for (int x0 = 0; x0 < S.n_launched; x0 += 8) {

@@ -43,6 +43,11 @@ struct DecodeParams {
   const __nv_bfloat16* v;
   long long v_sb, v_sh, v_ss;
   int B, H, Hkv, G, n_keys;
+  // optional device key count (CUDA-graph replays with a growing cache): the
+  // kernels read the live count n = clamp(*n_keys_dev, 1, n_keys) and n_keys
+  // is the capacity the grids are sized for; all_sparse is then decided per
+  // call on the device (n <= sink + window)
+  const int* n_keys_dev;
   float scale_log2;
   int window, sink, all_sparse;
   DecodeSet set[2];        // 0: dense (every key), 1: sparse

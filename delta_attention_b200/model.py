@@ -197,7 +197,12 @@ class DeltaDecoder:
             out, _ = plug.sdpa_rectangle_forward(plug, q, k, v, None, scaling=self.scaling)
         return out
 
-    def _layer(self, i: int, x: torch.Tensor, pos0: int, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    def _layer(self, i: int, x: torch.Tensor, pos0: int, cos: torch.Tensor, sin: torch.Tensor,
+               pos_t: Optional[torch.Tensor] = None, attend: Optional[Callable] = None) -> torch.Tensor:
+        """One decoder layer.  ``pos_t`` (a device position, one new token)
+        and ``attend(i, q, k_cache, v_cache)`` select the graph-replayed decode
+        step: the cache write and the attention then take the position from
+        device memory and the attention reads the whole cache."""
         a, layer = self.arch, self.layers[i]
         B, s, D = x.shape
         d = a.head_dim
@@ -218,11 +223,16 @@ class DeltaDecoder:
         k = k * c + rotate_half(k) * sn
         # KV-cache write path: post-RoPE keys and values at positions [pos0, pos0 + s)
         kc, vc = self.k_cache[i], self.v_cache[i]
-        kc[:, :, pos0:pos0 + s] = k.transpose(1, 2)
-        vc[:, :, pos0:pos0 + s] = v.transpose(1, 2)
-        n = pos0 + s
-        with self._timed("attention"):
-            o = self._attend(i, layer, q.transpose(1, 2), kc[:, :, :n], vc[:, :, :n], prefill=(pos0 == 0))
+        if pos_t is not None:
+            kc.index_copy_(2, pos_t, k.transpose(1, 2))
+            vc.index_copy_(2, pos_t, v.transpose(1, 2))
+            o = attend(i, q.transpose(1, 2), kc, vc)
+        else:
+            kc[:, :, pos0:pos0 + s] = k.transpose(1, 2)
+            vc[:, :, pos0:pos0 + s] = v.transpose(1, 2)
+            n = pos0 + s
+            with self._timed("attention"):
+                o = self._attend(i, layer, q.transpose(1, 2), kc[:, :, :n], vc[:, :, :n], prefill=(pos0 == 0))
         with self._timed("gemm"):
             o = o.reshape(B, s, self.Hl * d) @ layer["w_o"].t()
         with self._timed("all_reduce"):
@@ -279,6 +289,121 @@ class DeltaDecoder:
     def decode_step(self, tokens: torch.Tensor) -> torch.Tensor:
         """One new token per sequence [B] -> the next token [B]."""
         return self._next_token(self.forward(tokens[:, None])[:, -1])
+
+
+class DecodeGraph:
+    """Greedy decode with one CUDA-graph replay per token.
+
+    One decode step of the whole model (every layer's projections, RoPE,
+    KV-cache write, attention, all-reduces, the LM head and the next-token
+    choice) is captured once and replayed; the input token, the position and
+    the live cache length are device tensors that the graph advances itself,
+    so the host issues one replay per token instead of hundreds of launches.
+    The attention is the plug-in's decode kernel with the key count read from
+    device memory (``ops.decode(..., n_keys_dev=)``) over the whole cache.
+    Modes: dense, sparse, and delta with the fixed refresh schedule (anchor
+    every ``min(gamma_dec, gamma_dec_max)`` steps, ``delta_attention/llama.py:552-634``):
+    delta mode captures an anchor step (dense and sparse rows, delta refreshed,
+    output = dense) and a sparse step (output = sparse + delta), and the host
+    picks the graph by the step count.  Drift policies and drift logging
+    decide from device values on the host and use the eager path
+    (:meth:`DeltaDecoder.decode_step`)."""
+
+    def __init__(self, model: "DeltaDecoder", batch: int):
+        cfg = model.cfg
+        self.model, self.batch = model, batch
+        self.mode = getattr(cfg, "decode_mode", "dense")
+        if self.mode == "delta" and (getattr(cfg, "refresh_policy", "fixed") != "fixed"
+                                     or getattr(cfg, "log_drift", False)):
+            raise ValueError("graph decode supports the fixed refresh schedule without drift logging")
+        self.period = max(1, min(int(getattr(cfg, "gamma_dec", 32)), int(getattr(cfg, "gamma_dec_max", 128))))
+        self.window = int(cfg.sliding_window)
+        self.sink = int(getattr(cfg, "sink", 1024))
+        dev, d = model.device, model.arch.head_dim
+        self.tok = torch.zeros(batch, dtype=torch.long, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.long, device=dev)
+        self.n_keys = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.hidden = torch.zeros(batch, model.arch.hidden, dtype=model.dtype, device=dev)  # last step's output
+        self.delta = [torch.zeros(batch, 1, model.Hl, d, dtype=torch.bfloat16, device=dev) for _ in model.layers] \
+            if self.mode == "delta" else []
+        self.graphs: Dict[bool, torch.cuda.CUDAGraph] = {}
+        self.steps = 0
+
+    def _attend(self, anchor: bool):
+        from . import ops
+
+        m = self.model
+
+        def attend(i, q, kc, vc):
+            kw = dict(window=self.window, sink=self.sink, scaling=m.scaling, n_keys_dev=self.n_keys)
+            if self.mode == "dense":
+                out, _ = ops.decode(q, kc, vc, want_dense=True, want_sparse=False, **kw)
+            elif self.mode == "sparse":
+                _, out = ops.decode(q, kc, vc, want_dense=False, want_sparse=True, **kw)
+            elif anchor:
+                dense, sparse = ops.decode(q, kc, vc, want_dense=True, want_sparse=True, **kw)
+                self.delta[i].copy_(dense - sparse)
+                out = dense
+            else:
+                _, sparse = ops.decode(q, kc, vc, want_dense=False, want_sparse=True, **kw)
+                out = sparse + self.delta[i]
+            return out
+
+        return attend
+
+    def _step(self, anchor: bool) -> None:
+        m = self.model
+        x = m.embed[self.tok][:, None, :]
+        cos, sin = cos_sin(self.pos, *m._rope)
+        attend = self._attend(anchor)
+        for i in range(len(m.layers)):
+            x = m._layer(i, x, 0, cos, sin, pos_t=self.pos, attend=attend)
+        self.hidden.copy_(x[:, -1])
+        self.tok.copy_(m._next_token(x[:, -1]))
+        self.pos.add_(1)
+        self.n_keys.add_(1)
+
+    def _capture(self) -> None:
+        saved = (self.tok.clone(), self.pos.clone(), self.n_keys.clone())
+        for anchor in ((True, False) if self.mode == "delta" else (False,)):
+            # one eager run first (kernel attributes, library handles, NCCL
+            # communicators), then rewind the device state it advanced; the
+            # cache slot it wrote is written again by the first real step
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                self._step(anchor)
+            torch.cuda.current_stream().wait_stream(side)
+            for t, v in zip((self.tok, self.pos, self.n_keys), saved):
+                t.copy_(v)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._step(anchor)
+            self.graphs[anchor] = g
+
+    def start(self, first_token: torch.Tensor) -> None:
+        """Begin decoding after :meth:`DeltaDecoder.prefill` (which returned
+        ``first_token``): the next step writes cache position ``model.length``."""
+        m = self.model
+        self.tok.copy_(first_token)
+        self.pos.fill_(m.length)
+        self.n_keys.fill_(m.length + 1)
+        self.steps = 0
+        if not self.graphs:
+            self._capture()
+
+    def step(self) -> torch.Tensor:
+        """One token per sequence; returns the device tensor of the next token
+        (overwritten by the next step)."""
+        anchor = self.mode == "delta" and self.steps % self.period == 0
+        self.graphs[anchor].replay()
+        self.steps += 1
+        self.model.length += 1
+        return self.tok
+
+    def release(self) -> None:
+        """Drop the graphs (before a process group that they use is destroyed)."""
+        self.graphs.clear()
 
 
 class _NullCtx:

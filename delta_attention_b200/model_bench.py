@@ -41,6 +41,9 @@ def parse_args(argv=None):
     ap.add_argument("--gamma-dec", type=int, default=32)
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (0 = the architecture's)")
     ap.add_argument("--breakdown-steps", type=int, default=8)
+    ap.add_argument("--eager-decode", action="store_true",
+                    help="decode through the eager path (one launch sequence per layer from Python) "
+                         "instead of one CUDA-graph replay per token")
     return ap.parse_args(argv)
 
 
@@ -68,7 +71,7 @@ def main(argv=None) -> int:
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     from . import ops
     from .config import Config
-    from .model import ARCHS, TP, DeltaDecoder, tiny
+    from .model import ARCHS, TP, DecodeGraph, DeltaDecoder, tiny
 
     arch = ARCHS[args.arch]
     if args.layers:
@@ -80,11 +83,15 @@ def main(argv=None) -> int:
     ids = torch.randint(0, arch.vocab, (args.batch, args.seq), generator=g, device=dev)
     model.allocate_cache(args.batch, args.seq + args.new_tokens + args.breakdown_steps + 1)
 
-    # warm-up: a short prompt and a few steps (kernels, cuBLAS heuristics, NCCL)
+    # warm-up: a short prompt and a few steps (kernels, cuBLAS heuristics, NCCL;
+    # the decode graphs are captured here)
+    graph = None if args.eager_decode else DecodeGraph(model, args.batch)
     warm = ids[:, :min(args.seq, 8192)]
     tok = model.prefill(warm)
+    if graph is not None:
+        graph.start(tok)
     for _ in range(3):
-        tok = model.decode_step(tok)
+        tok = graph.step() if graph is not None else model.decode_step(tok)
     torch.cuda.synchronize()
     ops.check_errors()
 
@@ -105,8 +112,14 @@ def main(argv=None) -> int:
     barrier()
     d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     d0.record()
-    for _ in range(args.new_tokens):
-        tok = model.decode_step(tok)
+    if graph is not None:
+        graph.start(tok)
+        for _ in range(args.new_tokens):
+            graph.step()
+        tok = graph.tok.clone()
+    else:
+        for _ in range(args.new_tokens):
+            tok = model.decode_step(tok)
     d1.record()
     torch.cuda.synchronize()
     dec_ms = d0.elapsed_time(d1)
@@ -141,6 +154,7 @@ def main(argv=None) -> int:
             "window": args.window, "sink": args.sink, "gamma": args.gamma,
             "ttft_ms": ttft,
             "prefill_tokens_per_s": args.batch * args.seq / (ttft / 1e3),
+            "decode_path": "eager" if args.eager_decode else "cuda graph per token",
             "decode_ms_per_step": dec_ms / args.new_tokens,
             "decode_tokens_per_s": args.batch * args.new_tokens / (dec_ms / 1e3),
             "prefill_breakdown_ms": pre, "decode_breakdown_ms_per_step": dec,
@@ -149,6 +163,8 @@ def main(argv=None) -> int:
             "data": "synthetic (uniform-random token ids, seeded random-init weights)",
         }
         print(json.dumps(line), flush=True)
+    if graph is not None:
+        graph.release()  # graphs holding NCCL work go before the process group
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

@@ -332,10 +332,14 @@ def _decode_workspace(nbytes: int, device) -> torch.Tensor:
 
 def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, window: int, sink: int,
            scaling: Optional[float] = None, want_dense: bool = True, want_sparse: bool = True,
-           n_keys: Optional[int] = None) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor]]:
+           n_keys: Optional[int] = None, n_keys_dev: Optional[torch.Tensor] = None,
+           ) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor]]:
     """One decode row per (batch, head).  q [b, H, 1, d]; k/v [b, Hkv, n, d]
     (only the first ``n_keys`` keys are used).  Returns ``(dense, sparse)``,
-    each [b, 1, H, d] bf16 or None; both come from one pass over the cache."""
+    each [b, 1, H, d] bf16 or None; both come from one pass over the cache.
+    ``n_keys_dev`` (a device int32 scalar tensor) gives the live key count on
+    the device instead: k/v are then the whole cache (its capacity sizes the
+    launch), so a CUDA graph can replay the call while the cache grows."""
     _check_cuda(q, k, v)
     qb, kb, vb = _bf16_lastdim_contig(q), _bf16_lastdim_contig(k), _bf16_lastdim_contig(v)
     b, H, one, d = qb.shape
@@ -358,6 +362,10 @@ def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, window: int, si
     a.scaling = float(scaling)
     a.window, a.sink = int(window), int(sink)
     a.dense_out, a.sparse_out = _ptr(dense), _ptr(sparse)
+    if n_keys_dev is not None:
+        if n_keys_dev.dtype != torch.int32 or n_keys_dev.device != q.device or n_keys_dev.numel() != 1:
+            raise ValueError("n_keys_dev must be a one-element int32 tensor on q's device")
+        a.n_keys, a.n_keys_dev = kb.shape[2], _ptr(n_keys_dev)
     ws = _decode_workspace(lib().dta_decode_workspace_size(ctypes.byref(a)), q.device)
     a.workspace, a.workspace_bytes = _ptr(ws), ws.numel()
     _check_status(lib().dta_decode(ctypes.byref(a), ctypes.c_void_p(_stream())), "dta_decode")

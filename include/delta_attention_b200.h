@@ -190,6 +190,9 @@ typedef struct dta_decode_args {
   void* sparse_out;
   void* workspace;
   size_t workspace_bytes;
+  const int32_t* n_keys_dev; /* optional device int32: the live key count, read by the kernels (clamped to
+                                [1, n_keys]); n_keys is then the cache capacity the launch is sized for.
+                                Lets a CUDA graph replay the same call while the cache grows. */
 } dta_decode_args;
 DTA_API size_t dta_decode_workspace_size(const dta_decode_args* args);
 DTA_API int dta_decode(const dta_decode_args* args, void* stream);

@@ -140,3 +140,39 @@ def test_tp_decoder_matches_transformers_model(arch):
     _close_logits(got, ref, f"{arch} DeltaDecoder vs transformers")
     from delta_attention_b200 import ops
     ops.check_errors()
+
+
+@pytest.mark.parametrize("mode", ["dense", "sparse", "delta"])
+def test_graph_decode_matches_eager_decode(mode):
+    """One CUDA-graph replay per token (model.DecodeGraph: the step captured
+    with the position and the cache length in device memory) gives the same
+    hidden states as the eager decode path, teacher-forced on the graph's own
+    tokens, in every decode mode (delta: anchors every gamma_dec steps)."""
+    from delta_attention_b200.config import Config
+    from delta_attention_b200.model import LLAMA31_8B, DecodeGraph, DeltaDecoder, tiny
+
+    arch = tiny(LLAMA31_8B, n_layers=2, hidden=512, n_heads=8, n_kv_heads=2, head_dim=64, intermediate=1024,
+                vocab=1000)
+    cfg = Config(delta_lambda=GAMMA, sliding_window=WINDOW, sink=SINK, mode="delta", decode_mode=mode,
+                 gamma_dec=3)
+    eager = DeltaDecoder(arch, cfg, device="cuda", seed=3)
+    graphed = DeltaDecoder(arch, cfg, device="cuda", seed=3)
+    ids = torch.randint(0, arch.vocab, (2, SEQ), generator=torch.Generator().manual_seed(5)).cuda()
+    steps = 7
+    for m in (eager, graphed):
+        m.allocate_cache(2, SEQ + steps + 8)
+    t0 = eager.prefill(ids)
+    assert torch.equal(t0, graphed.prefill(ids))
+    g = DecodeGraph(graphed, batch=2)
+    g.start(t0)
+    tok = t0
+    for i in range(steps):
+        g.step()
+        h_graph = g.hidden.clone()
+        h_eager = eager.forward(tok[:, None])[:, -1]
+        tok = g.tok.clone()
+        err = (h_graph.float() - h_eager.float()).abs().max().item()
+        cos = torch.nn.functional.cosine_similarity(h_graph.float().flatten(), h_eager.float().flatten(), dim=0)
+        assert err <= 5e-2 and cos.item() >= 0.9999, f"{mode} step {i}: max abs {err:.3e}, cos {cos.item():.6f}"
+    assert graphed.length == eager.length
+    g.release()
