@@ -576,7 +576,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
             const int hh = m >> r_shift, rr = m & (p.R - 1);
             const int head = J.g * p.G + hh;
             const int row = qt * p.R + rr;
-            float lse = INFINITY, dv = 0.f;
+            float lse = INFINITY, dv = 0.f;  // (columns the tile does not have)
             if (!dense && row < p.s_p) {
               const long long o = ((long long)J.b * p.H + head) * p.S + row;
               lse = p.lse_sp[o];
@@ -586,7 +586,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
               lse = p.lse_dn[o];
               dv = p.d_dn[o];
             }
-            stats[m] = lse;
+            stats[m] = -lse;  // negated: the compute warps form s * scale - lse with one packed fma
             stats[128 + m] = dv;
           }
           __syncwarp();
@@ -852,9 +852,15 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
           }
           tc_fence_after();
           const int kt = u < J.n0 ? u : J.w0 + (u - J.n0);
+          // the dQ product two iterations back has read this iteration's dS buffer
+          if (!mbar_wait_warp(BBAR(ds_free[0]) + 8 * (n & 1), ((n >> 1) & 1) ^ 1, wc, KERR_TIMEOUT_SOFTMAX)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
           // 32 columns at a time; S and dP are released once the second
           // chunk is in registers (the first chunk's dS is formed meanwhile)
-          uint32_t pk[32];
+          const uint64_t sl2x2 = f2_pack(sl2, sl2);
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             float sv[32], dv[32];
@@ -869,20 +875,21 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
             const int kb = kt * BWD_BN + wg * 64 + c * 32;
             uint32_t m = qvalid ? bits_range(0, qpos - kb + 1) : 0u;
             if (p.pass == BWD_SPARSE) m &= bits_range(0, p.sink - kb) | bits_range(qlo - kb, 32);
+            // P = exp2(s * scale - lse) and dS = P (dP - D) on packed fp32 pairs
+            uint32_t pk[16];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              const float p0 = ((m >> e) & 1u) ? fast_exp2(sv[e] * sl2 - qlse) : 0.f;
-              const float p1 = ((m >> (e + 1)) & 1u) ? fast_exp2(sv[e + 1] * sl2 - qlse) : 0.f;
-              pk[c * 16 + (e >> 1)] = pack_bf16x2(p0 * (dv[e] - qd), p1 * (dv[e + 1] - qd));
+              float a0, a1;
+              f2_unpack(f2_fma(f2_pack(sv[e], sv[e + 1]), sl2x2, f2_pack(-qlse, -qlse)), a0, a1);
+              const float p0 = ((m >> e) & 1u) ? fast_exp2(a0) : 0.f;
+              const float p1 = ((m >> (e + 1)) & 1u) ? fast_exp2(a1) : 0.f;
+              float d0, d1;
+              f2_unpack(f2_mul(f2_pack(p0, p1), f2_sub(f2_pack(dv[e], dv[e + 1]), f2_pack(qd, qd))), d0, d1);
+              pk[e >> 1] = pack_bf16x2(d0, d1);
             }
+            __syncwarp();
+            tmem_st16(tmem + lane_off + G::DS + (n & 1) * 64 + wg * 32 + c * 16, pk);
           }
-          // the dQ product two iterations back has read this dS buffer
-          if (!mbar_wait_warp(BBAR(ds_free[0]) + 8 * (n & 1), ((n >> 1) & 1) ^ 1, wc, KERR_TIMEOUT_SOFTMAX)) {
-            aborted = true;
-            break;
-          }
-          tc_fence_after();
-          tmem_st32(tmem + lane_off + G::DS + (n & 1) * 64 + wg * 32, pk);
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
@@ -928,24 +935,28 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
             if (p.pass == BWD_SPARSE) m &= bits_range(0, p.sink - kb) | bits_range(qlo - kb, 32);
           }
           uint32_t pk[16], dk[16];
+          // P = exp2(s * scale - lse) and dS = P (dP - D) on packed fp32 pairs;
+          // the query rows' -lse and D come four at a time from the stage's stats
+          const uint64_t sl2x2 = f2_pack(sl2, sl2);
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float p0, p1, d0, d1;
-            if constexpr (KM) {
-              const float l0 = stats[col0 + e], l1 = stats[col0 + e + 1];
-              const float q0 = stats[128 + col0 + e], q1 = stats[128 + col0 + e + 1];
-              p0 = ((m >> e) & 1u) ? fast_exp2(s[e] * sl2 - l0) : 0.f;
-              p1 = ((m >> (e + 1)) & 1u) ? fast_exp2(s[e + 1] * sl2 - l1) : 0.f;
-              d0 = p0 * (dp[e] - q0);
-              d1 = p1 * (dp[e + 1] - q1);
-              pk[e >> 1] = pack_bf16x2(p0, p1);
-            } else {
-              p0 = ((m >> e) & 1u) ? fast_exp2(s[e] * sl2 - qlse) : 0.f;
-              p1 = ((m >> (e + 1)) & 1u) ? fast_exp2(s[e + 1] * sl2 - qlse) : 0.f;
-              d0 = p0 * (dp[e] - qd);
-              d1 = p1 * (dp[e + 1] - qd);
+          for (int e = 0; e < 32; e += 4) {
+            const float4 nl4 = *reinterpret_cast<const float4*>(stats + col0 + e);
+            const float4 dd4 = *reinterpret_cast<const float4*>(stats + 128 + col0 + e);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int f = e + 2 * h;
+              const uint64_t nl = h ? f2_pack(nl4.z, nl4.w) : f2_pack(nl4.x, nl4.y);
+              const uint64_t dd = h ? f2_pack(dd4.z, dd4.w) : f2_pack(dd4.x, dd4.y);
+              float a0, a1;
+              f2_unpack(f2_fma(f2_pack(s[f], s[f + 1]), sl2x2, nl), a0, a1);
+              const float p0 = ((m >> f) & 1u) ? fast_exp2(a0) : 0.f;
+              const float p1 = ((m >> (f + 1)) & 1u) ? fast_exp2(a1) : 0.f;
+              const uint64_t p2 = f2_pack(p0, p1);
+              float d0, d1;
+              f2_unpack(f2_mul(p2, f2_sub(f2_pack(dp[f], dp[f + 1]), dd)), d0, d1);
+              pk[f >> 1] = pack_bf16x2(p0, p1);
+              dk[f >> 1] = pack_bf16x2(d0, d1);
             }
-            dk[e >> 1] = pack_bf16x2(d0, d1);
           }
           __syncwarp();
           if constexpr (KM) {
