@@ -404,6 +404,7 @@ def run_train(args, local_rank):
     flops = 3.5 * fwd_flops
 
     def step():
+        q.grad = k.grad = v.grad = None  # gradients are assigned, not accumulated (as after zero_grad)
         out = train.delta_forward_train(q, k, v, args.gamma, args.window, args.sink)
         out.backward(g)
         return out
@@ -416,6 +417,7 @@ def run_train(args, local_rank):
     with sampler:
         for _ in range(max(1, args.steps)):
             flush.zero_()
+            q.grad = k.grad = v.grad = None
             e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
             e[0].record()
             out = train.delta_forward_train(q, k, v, args.gamma, args.window, args.sink)
