@@ -22,20 +22,25 @@
 //                      D, and q of the dense rows in list order (so every tile
 //                      load is one TMA box)
 //   backward_plan    : per key tile, the first job of the key-major launch
-//   bwd_kernel<KM>   : key-major: a job is one key tile (128 keys of one KV
-//                      group) and a chunk of the query tiles that attend it;
-//                      dK, dV accumulate in TMEM and leave with fp32 vector
-//                      atomics (a key tile's chunks may run on several SMs)
-//   bwd_kernel<QM>   : query-major, two launches (dense rows, then windowed
-//                      rows): a job is one query tile over its key tiles; dQ
-//                      accumulates in TMEM; the windowed launch adds the dense
-//                      launch's dQ of each anchor row
+//   bwd_kernel<QM>   : query-major, dense rows: a job is one list tile over
+//                      its key tiles; dQ accumulates in TMEM (anchor rows to an
+//                      fp32 buffer, tail rows to grad_q)
+//   bwd_kernel<KM>   : key-major, queued as a programmatic dependent launch of
+//                      the one before: a job is one key tile (128 keys of one
+//                      KV group) and a chunk of the query tiles that attend
+//                      it; dK, dV accumulate in TMEM and leave with fp32
+//                      vector atomics (a key tile's chunks may run on several SMs)
+//   bwd_kernel<QM>   : query-major, windowed rows (adds the dense rows' dQ of
+//                      each anchor row)
 //   backward_finalize: dK (times scale), dV to bf16
 // Per (query tile, key tile) both tcgen05 kernels run S and dP as two
-// SS-form 128 x 128 x d products, form P and dS in registers (two compute
-// warpgroups, 64 columns each), write them back over S / dP in TMEM as bf16
-// and feed them to TS-form products (A from TMEM, B an MN-major view of the
-// shared-memory tile that S and dP read K-major).
+// SS-form 128 x 128 x d products and form P and dS in registers (two compute
+// warpgroups, 64 columns each, packed fp32 pairs).  Key-major: P^T and dS^T
+// go back over S^T / dP^T in TMEM as bf16 and feed TS-form products (A from
+// TMEM, B an MN-major view of the shared-memory tile that S^T and dP^T read
+// K-major).  Query-major: dS goes to one of two spare TMEM buffers, so the
+// next key tile's S and dP are issued as soon as this tile's are in registers
+// and run while dS is formed.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -281,9 +286,9 @@ cudaError_t launch_backward_finalize(const float* dk_acc, const float* dv_acc, _
 //   warps 2, 3  idle
 //   warps 4..11 two compute warpgroups; warpgroup w owns columns [64 w, 64 w + 64)
 //               of S and dP (TMEM lane = the thread's tile row)
-// TMEM: T1 [0, 128) S or S^T, then bf16 dS (query-major) / P^T (key-major) in
-// place; T2 [128, 256) dP or dP^T, then bf16 dS^T (key-major) in place;
-// accumulators from column 256: dQ, or dV then dK.
+// TMEM: T1 [0, 128) S or S^T (key-major: then bf16 P^T in place); T2 [128,
+// 256) dP or dP^T (key-major: then bf16 dS^T in place); accumulators from
+// column 256: dQ, or dV then dK; query-major: bf16 dS buffers at 384 and 448.
 constexpr int BWD_THREADS = 384;
 constexpr int BWD_CTRL = 1024;
 enum BwdKind : int { BWD_QM = 0, BWD_KM = 1 };
@@ -467,6 +472,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
     tma_prefetch_desc(&p.tm_gsp);
     tma_prefetch_desc(&p.tm_gdn);
   }
+  // the dense-row dQ launch lets the key-major launch queued behind it start
+  // its CTAs as this grid's CTAs finish (its longest job, the tail rows over
+  // every key tile, would otherwise leave most SMs idle at the end)
+  if (!KM && p.pass == BWD_DENSE && threadIdx.x == 0) grid_dependents_launch();
   __syncwarp();
   if (warp == 1) {
     tmem_alloc(BBAR(tmem_base), 512);
@@ -1048,6 +1057,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
     }
   }
 #undef BBAR
+  // a key-major CTA never completes before the grid it may overlap (the
+  // dense-row dQ launch), so work queued after this launch sees that grid done
+  if (KM && threadIdx.x == 0) grid_dependency_wait();
   __syncwarp();
   tc_fence_before();
   __syncthreads();
@@ -1059,19 +1071,30 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
 }
 
 template <int HD, int KIND>
-static cudaError_t launch_bwd_hd(const BackwardParams& p, int grid, cudaStream_t stream) {
+static cudaError_t launch_bwd_hd(const BackwardParams& p, int grid, bool dependent, cudaStream_t stream) {
   const int smem = KIND == BWD_KM ? BGeo<HD>::SMEM : BGeo<HD>::SMEM_QM;
   cudaError_t e = cudaFuncSetAttribute(bwd_kernel<HD, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  bwd_kernel<HD, KIND><<<grid, BWD_THREADS, smem, stream>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(BWD_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = dependent ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, bwd_kernel<HD, KIND>, p);
 }
 
 cudaError_t launch_backward_dq(const BackwardParams& p, int head_dim, int grid, cudaStream_t stream) {
-  return head_dim == 128 ? launch_bwd_hd<128, BWD_QM>(p, grid, stream) : launch_bwd_hd<64, BWD_QM>(p, grid, stream);
+  return head_dim == 128 ? launch_bwd_hd<128, BWD_QM>(p, grid, false, stream)
+                         : launch_bwd_hd<64, BWD_QM>(p, grid, false, stream);
 }
-cudaError_t launch_backward_dkdv(const BackwardParams& p, int head_dim, int grid, cudaStream_t stream) {
-  return head_dim == 128 ? launch_bwd_hd<128, BWD_KM>(p, grid, stream) : launch_bwd_hd<64, BWD_KM>(p, grid, stream);
+cudaError_t launch_backward_dkdv(const BackwardParams& p, int head_dim, int grid, bool dependent, cudaStream_t stream) {
+  return head_dim == 128 ? launch_bwd_hd<128, BWD_KM>(p, grid, dependent, stream)
+                         : launch_bwd_hd<64, BWD_KM>(p, grid, dependent, stream);
 }
 
 }  // namespace dta
@@ -1227,31 +1250,32 @@ int dta_backward(const dta_backward_args* a, void* stream_) {
   if ((e = dta::launch_backward_plan(chunk_base, L.n_ktiles, S, L.s_p, L.n_anchor, L.n_sel, a->gamma, a->window,
                                      a->sink, a->q_block, R, kBwdChunkIters, stream)) != cudaSuccess)
     return dta::fail_cuda(e);
-  // dK, dV (key-major)
+  // dQ of the dense rows first (its longest job spans every key tile), the
+  // key-major dK / dV launch queued behind it as a programmatic dependent
+  // launch (independent of its output; its CTAs take SMs as the dense grid's
+  // finish), then dQ of the windowed rows, which adds the dense rows' dQ at
+  // each anchor row
+  dta::BackwardParams q = p;
+  q.counter = reinterpret_cast<int*>(ws) + 2;
+  q.pass = dta::BWD_DENSE;
+  q.n_qtiles = (L.n_sel + R - 1) / R;
+  q.n_jobs = q.n_qtiles * B * Hkv;
+  if ((e = dta::launch_backward_dq(q, d, q.n_jobs < sms ? q.n_jobs : sms, stream)) != cudaSuccess)
+    return dta::fail_cuda(e);
   {
     dta::BackwardParams k = p;
     k.counter = reinterpret_cast<int*>(ws) + 0;
     k.n_jobs = total_chunks * B * Hkv;
-    if (k.n_jobs > 0 && (e = dta::launch_backward_dkdv(k, d, k.n_jobs < sms ? k.n_jobs : sms, stream)) != cudaSuccess)
+    if (k.n_jobs > 0 && (e = dta::launch_backward_dkdv(k, d, k.n_jobs < sms ? k.n_jobs : sms, true, stream)) !=
+                            cudaSuccess)
       return dta::fail_cuda(e);
   }
-  // dQ: the dense rows, then the windowed rows (which add the dense pass's
-  // dQ of each anchor row)
-  {
-    dta::BackwardParams q = p;
-    q.counter = reinterpret_cast<int*>(ws) + 2;
-    q.pass = dta::BWD_DENSE;
-    q.n_qtiles = (L.n_sel + R - 1) / R;
-    q.n_jobs = q.n_qtiles * B * Hkv;
-    if ((e = dta::launch_backward_dq(q, d, q.n_jobs < sms ? q.n_jobs : sms, stream)) != cudaSuccess)
-      return dta::fail_cuda(e);
-    q.counter = reinterpret_cast<int*>(ws) + 3;
-    q.pass = dta::BWD_SPARSE;
-    q.n_qtiles = (L.s_p + R - 1) / R;
-    q.n_jobs = q.n_qtiles * B * Hkv;
-    if ((e = dta::launch_backward_dq(q, d, q.n_jobs < sms ? q.n_jobs : sms, stream)) != cudaSuccess)
-      return dta::fail_cuda(e);
-  }
+  q.counter = reinterpret_cast<int*>(ws) + 3;
+  q.pass = dta::BWD_SPARSE;
+  q.n_qtiles = (L.s_p + R - 1) / R;
+  q.n_jobs = q.n_qtiles * B * Hkv;
+  if ((e = dta::launch_backward_dq(q, d, q.n_jobs < sms ? q.n_jobs : sms, stream)) != cudaSuccess)
+    return dta::fail_cuda(e);
   const long long n = (long long)B * Hkv * S * d;
   if ((e = dta::launch_backward_finalize(p.dk_acc, p.dv_acc, reinterpret_cast<__nv_bfloat16*>(a->grad_k),
                                          reinterpret_cast<__nv_bfloat16*>(a->grad_v), n, a->scaling, stream)) !=

@@ -114,7 +114,10 @@ cudaError_t launch_backward_prep(const __nv_bfloat16* q, long long q_sb, long lo
 cudaError_t launch_backward_plan(int* chunk_base, int n_ktiles, int S, int s_p, int n_anchor, int n_sel, int gamma,
                                  int window, int sink, int qblock, int R, int chunk_iters, cudaStream_t stream);
 cudaError_t launch_backward_dq(const BackwardParams& p, int head_dim, int grid, cudaStream_t stream);
-cudaError_t launch_backward_dkdv(const BackwardParams& p, int head_dim, int grid, cudaStream_t stream);
+// `dependent`: queued as a programmatic dependent launch of the launch before
+// it on the stream (its CTAs may start while that grid runs; each waits for it
+// before exiting)
+cudaError_t launch_backward_dkdv(const BackwardParams& p, int head_dim, int grid, bool dependent, cudaStream_t stream);
 // dk = scaling * dk_acc, dv = dv_acc, both to bf16 [B, Hkv, S, d]
 cudaError_t launch_backward_finalize(const float* dk_acc, const float* dv_acc, __nv_bfloat16* dk, __nv_bfloat16* dv,
                                      long long n, float scaling, cudaStream_t stream);

@@ -116,6 +116,23 @@ def test_backward_matches_oracle(case):
     _grad_check(vc.grad, vo.grad, "dv")
 
 
+def test_backward_config1_matches_oracle():
+    """The benchmark matrix's config 1 (s=4096, 32/8 heads, d=128, W=1024, S=64,
+    gamma=64; the reference's CPU-runnable training shape): every gradient
+    against the oracle's float64 autograd on the same bf16 inputs."""
+    s, H, Hkv, d, gamma, window, sink = 4096, 32, 8, 128, 64, 1024, 64
+    q, k, v = make_inputs(s, H, Hkv, d, seed=0, rope_theta=500000.0, dtype=torch.bfloat16)
+    gout = torch.randn(1, s, H, d, generator=torch.Generator().manual_seed(1)).bfloat16()
+    qo, ko, vo = (t.double().requires_grad_(True) for t in (q, k, v))
+    (orc.delta_forward_train(qo, ko, vo, gamma, window, sink) * gout.double()).sum().backward()
+    qc, kc, vc = (t.cuda().requires_grad_(True) for t in (q, k, v))
+    train.delta_forward_train(qc, kc, vc, gamma, window, sink).backward(gout.cuda())
+    ops.check_errors()
+    _grad_check(qc.grad, qo.grad, "config1 dq")
+    _grad_check(kc.grad, ko.grad, "config1 dk")
+    _grad_check(vc.grad, vo.grad, "config1 dv")
+
+
 def _t14_inputs(seed=0):
     torch.manual_seed(seed)
     q = torch.randn(1, 32, 4096, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
