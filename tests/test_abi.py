@@ -164,3 +164,54 @@ def test_anchor_delta_in_needs_explicit_anchors():
     a.anchor_delta_in = 1 << 21  # uniform anchors: refused
     assert L.dta_prefill(ctypes.byref(a), None) == 1
     assert L.dta_prefill_workspace_size(ctypes.byref(a)) == 0
+
+
+def _backward_args(**kw):
+    a = _lib.BackwardArgs()
+    a.abi_version = _lib.ABI_VERSION
+    a.batch, a.n_heads, a.n_kv_heads, a.seq_len, a.head_dim = 1, 32, 8, 4096, 128
+    fake = 1 << 20  # never dereferenced: validation fails before any CUDA call
+    a.q = a.k = a.v = a.out = a.grad_out = a.anchor_delta = a.lse_sparse = a.lse_dense = fake
+    a.grad_q = a.grad_k = a.grad_v = fake
+    a.q_stride_b, a.q_stride_h, a.q_stride_s = 32 * 4096 * 128, 4096 * 128, 128
+    a.k_stride_b, a.k_stride_h, a.k_stride_s = 8 * 4096 * 128, 4096 * 128, 128
+    a.v_stride_b, a.v_stride_h, a.v_stride_s = 8 * 4096 * 128, 4096 * 128, 128
+    a.scaling = 128 ** -0.5
+    a.gamma, a.window, a.sink, a.q_block = 64, 1024, 64, 64
+    a.delta_grad_scale = 1.0
+    for k_, v_ in kw.items():
+        setattr(a, k_, v_)
+    return a
+
+
+@pytest.mark.parametrize("override,status", [
+    (dict(gamma=48), 5),          # s_p % gamma != 0
+    (dict(seq_len=128), 5),       # no anchor row (s_p = 0)
+    (dict(head_dim=96), 6),
+    (dict(n_kv_heads=2), 2),      # 16 query heads per KV head: not 1, 2, 4 or 8
+    (dict(q_block=0), 1),
+    (dict(delta_grad_scale=float("nan")), 1),
+    (dict(abi_version=2), 1),
+    (dict(workspace_bytes=0), 7),  # (size checked before any pointer use)
+])
+def test_backward_validation_status(override, status):
+    L = _lib.lib()
+    a = _backward_args(**override)
+    assert L.dta_backward(ctypes.byref(a), None) == status
+
+
+def test_backward_workspace_size():
+    """Header, key-major chunk table, the two passes' output gradients (bf16),
+    q of the dense rows, row sums and the dense rows' dQ, fp32 dK / dV; each
+    section 256-byte aligned (dta_backward.cu backward_layout)."""
+    L = _lib.lib()
+    a = _backward_args()
+    s, H, Hkv, d, g = 4096, 32, 8, 128, 64
+    cut = s % g + max(128, g)
+    s_p = s - cut
+    n_a, n_sel = s_p // g, s_p // g + cut
+    al = lambda x: (x + 255) // 256 * 256
+    want = (256 + al((-(-s // 128) + 1) * 4) + al(s_p * H * d * 2) + al(n_sel * H * d * 2) + al(H * n_sel * d * 2)
+            + al(H * s * 4) + al(H * n_sel * 4) + al(H * n_a * d * 4) + 2 * al(Hkv * s * d * 4))
+    assert L.dta_backward_workspace_size(ctypes.byref(a)) == want
+    assert L.dta_backward_workspace_size(ctypes.byref(_backward_args(gamma=48))) == 0
