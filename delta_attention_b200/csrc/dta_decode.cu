@@ -6,10 +6,14 @@
 // (max, sum, o[d]) for its key set: DENSE (every key) or SPARSE (the first
 // `sink` keys plus the last `window` keys; delta_attention/llama.py:538-550).
 // A merge kernel combines the partials with the log-sum-exp rule.  An anchor
-// step of delta decode (delta_attention/llama.py:552-634) launches both key
-// sets in one grid (the sparse CTAs of chunks outside the sink and window exit
-// at once, the others re-read their chunk from L2); a non-anchor step launches
-// only the chunks that intersect the sparse key set.
+// step of delta decode (delta_attention/llama.py:552-634) launches the dense
+// set's grid and then the sparse set's, whose CTAs cover only the chunks that
+// intersect the sink and window and re-read them from L2; a non-anchor step
+// launches only the sparse grid.  The merge is a programmatic dependent launch
+// (DTA_DEC_PDL_MERGE): its CTAs become resident while the partial grid runs
+// and wait on the device for it, so no step pays the merge's launch latency
+// after the partials (same-box A/B: sparse 10.75 -> 10.24 us, anchor step
+// 94.5 -> 93.6 us, dense 85.9 -> 85.7 us).
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -17,28 +21,41 @@
 #include "dta_ptx.cuh"
 #include "dta_decode.h"
 
+// 0: plain merge launch; 1: programmatic dependent merge on sparse-only calls;
+// 2: on every call
+#ifndef DTA_DEC_PDL_MERGE
+#define DTA_DEC_PDL_MERGE 2
+#endif
+
 namespace dta {
 
 constexpr int DEC_THREADS = 128;
 
-// the live key count and whether every key is sparse (host values, or read
-// from the device count for CUDA-graph replays)
+// The live key count and whether every key is sparse: host values, or (DEVN,
+// a separate kernel instance) read from the device count for CUDA-graph
+// replays, so the host-count instance is free of the device-count logic.
+template <bool DEVN>
 __device__ __forceinline__ int dec_n_keys(const DecodeParams& p) {
-  return p.n_keys_dev ? min(max(*p.n_keys_dev, 1), p.n_keys) : p.n_keys;
+  if constexpr (DEVN) return min(max(*p.n_keys_dev, 1), p.n_keys);
+  return p.n_keys;
 }
+template <bool DEVN>
 __device__ __forceinline__ bool dec_all_sparse(const DecodeParams& p, int n) {
-  return p.n_keys_dev ? n <= p.sink + p.window : p.all_sparse != 0;
+  if constexpr (DEVN) return n <= p.sink + p.window;
+  return p.all_sparse != 0;
 }
 
 __device__ __forceinline__ bool dec_sparse_key(const DecodeParams& p, bool all_sparse, int n, int j) {
   return all_sparse || j < p.sink || j >= n - p.window;
 }
 
+template <bool DEVN>
 __device__ __forceinline__ int dec_chunk_of_block(const DecodeParams& p, const DecodeSet& S, bool all_sparse, int n,
                                                   int x) {
   if (!S.sparse || all_sparse) return x;
   // window chunks start at the chunk holding key n - window, after the sink chunks
-  const int fwc = p.n_keys_dev ? max(S.n_sink_chunks, max(n - p.window, 0) / S.chunk) : S.first_window_chunk;
+  int fwc = S.first_window_chunk;
+  if constexpr (DEVN) fwc = max(S.n_sink_chunks, max(n - p.window, 0) / S.chunk);
   return x < S.n_sink_chunks ? x : fwc + (x - S.n_sink_chunks);
 }
 
@@ -85,7 +102,7 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
-template <int HD>
+template <int HD, bool DEVN>
 __global__ void __launch_bounds__(DEC_THREADS) decode_mma_kernel(const __grid_constant__ DecodeParams p, int which) {
   constexpr int CH = HD / 8;                  // 16-byte chunks per row
   constexpr int ROWB = HD * 2;                // bytes per K/V row
@@ -95,16 +112,20 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_mma_kernel(const __grid_co
   // layout: [DEC_NSTAGE stages] x {K, V} x STAGE_BYTES; reused for the merge after the loop
   const uint32_t sbase = smem_u32(dsm);
 
+  // lets a programmatic dependent merge launch start its CTAs now; they wait
+  // in griddepcontrol.wait for this grid's completion and its memory flush
+  grid_dependents_launch();
   const DecodeSet& S = p.set[which];
-  const int n_live = dec_n_keys(p);
-  const bool all_sparse = dec_all_sparse(p, n_live);
-  const int c = dec_chunk_of_block(p, S, all_sparse, n_live, blockIdx.x);
+  const int n_live = dec_n_keys<DEVN>(p);
+  const bool all_sparse = dec_all_sparse<DEVN>(p, n_live);
+  const int c = dec_chunk_of_block<DEVN>(p, S, all_sparse, n_live, blockIdx.x);
   const int bg = blockIdx.y;
   const int b = bg / p.Hkv, g = bg - (bg / p.Hkv) * p.Hkv;
   const int G = p.G;
   const int k0 = c * S.chunk;
   const int k1 = min(k0 + S.chunk, n_live);
-  const int nk = max(k1 - k0, 0);  // 0: a chunk past the live keys (device count) leaves an empty partial
+  // (device count: a chunk past the live keys has none and leaves an empty partial)
+  const int nk = DEVN ? max(k1 - k0, 0) : k1 - k0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gr = lane >> 2, cq = lane & 3;  // fragment row (= head) and column pair
   float* part0 = S.partials + ((long long)(b * p.H + g * G) * S.n_launched + blockIdx.x) * (4 + HD);
@@ -258,17 +279,18 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_mma_kernel(const __grid_co
 
 // Merge the partials of every launched chunk of a key set: grid (B*H), block HD.
 // Chunk statistics are read in batches of 8 independent loads.
-template <int HD>
+template <int HD, bool DEVN>
 __global__ void decode_merge_kernel(const __grid_constant__ DecodeParams p) {
   const int bh = blockIdx.x;
   const int t = threadIdx.x;
+  grid_dependency_wait();  // no-op unless launched as a programmatic dependent
   for (int out = 0; out < 2; ++out) {
     __nv_bfloat16* dst = out == 0 ? p.dense_out : p.sparse_out;
     if (!dst) continue;
     // with n <= sink + window the two key sets coincide: both outputs come
     // from the sparse set's partials (host key count; with a device count the
     // dense output keeps the dense set, which covers the same keys)
-    const DecodeSet& S = p.set[(out == 1 || (!p.n_keys_dev && p.all_sparse)) ? 1 : 0];
+    const DecodeSet& S = p.set[DEVN ? out : (out == 1 || p.all_sparse) ? 1 : 0];
     const float* base = S.partials + (long long)bh * S.n_launched * (4 + HD);
     float M = -INFINITY;
     for (int x0 = 0; x0 < S.n_launched; x0 += 8) {
@@ -317,15 +339,26 @@ template <int HD>
 static cudaError_t launch_hd(const DecodeParams& p, cudaStream_t stream) {
   constexpr int smem = DEC_NSTAGE * 2 * DEC_STAGE * HD * 2;
   static_assert(smem >= (4 * 8 * HD + 4 * 2 * 8) * 4, "merge buffers fit in the stage buffers");
-  cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  auto kernel = p.n_keys_dev ? decode_mma_kernel<HD, true> : decode_mma_kernel<HD, false>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   const bool dense_set = p.dense_out && !p.all_sparse;
   const bool sparse_set = p.sparse_out || p.all_sparse;
-  if (dense_set)
-    decode_mma_kernel<HD><<<dim3(p.set[0].n_launched, p.B * p.Hkv), DEC_THREADS, smem, stream>>>(p, 0);
-  if (sparse_set)
-    decode_mma_kernel<HD><<<dim3(p.set[1].n_launched, p.B * p.Hkv), DEC_THREADS, smem, stream>>>(p, 1);
-  decode_merge_kernel<HD><<<p.B * p.H, HD, 0, stream>>>(p);
+  if (dense_set) kernel<<<dim3(p.set[0].n_launched, p.B * p.Hkv), DEC_THREADS, smem, stream>>>(p, 0);
+  if (sparse_set) kernel<<<dim3(p.set[1].n_launched, p.B * p.Hkv), DEC_THREADS, smem, stream>>>(p, 1);
+  const bool pdl = DTA_DEC_PDL_MERGE == 2 || (DTA_DEC_PDL_MERGE == 1 && !dense_set);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.B * p.H);
+  cfg.blockDim = dim3(HD);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  e = p.n_keys_dev ? cudaLaunchKernelEx(&cfg, decode_merge_kernel<HD, true>, p)
+                   : cudaLaunchKernelEx(&cfg, decode_merge_kernel<HD, false>, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
