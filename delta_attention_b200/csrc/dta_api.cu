@@ -539,28 +539,42 @@ int dta_rows(const dta_rows_args* a, void* stream_) {
   return DTA_OK;
 }
 
-// Chunking of one key set (dta::DecodeSet).
-static void decode_chunking(const dta_decode_args* a, int C, bool sparse, bool all_sparse, dta::DecodeSet* S) {
-  const int n = a->n_keys;
+// Chunking of one key set (dta::DecodeSet).  The dense set tiles [0, n) with
+// chunks of C keys.  The sparse set tiles [0, sink) from key 0 and
+// [n - window, n) from its first key, so its chunks hold only sparse keys;
+// with n <= sink + window it tiles [0, n) like the dense set.
+// With a device key count n_keys is the capacity: a capacity of at most
+// sink + window keeps every live count all-sparse ([0, n) in n_chunks chunks),
+// and above it the sink + window chunks also tile [0, n) for a live count of
+// at most sink + window.
+// Sink and window beyond the cache mean the whole cache: they are clamped to
+// n_keys (the same keys, and no int overflow in sink + window).
+static long long decode_sink(const dta_decode_args* a) { return a->sink < a->n_keys ? a->sink : a->n_keys; }
+static long long decode_window(const dta_decode_args* a) { return a->window < a->n_keys ? a->window : a->n_keys; }
+
+static void decode_chunking(const dta_decode_args* a, int C, bool sparse, dta::DecodeSet* S) {
+  const long long n = a->n_keys, sink = decode_sink(a), window = decode_window(a);
   S->chunk = C;
   S->sparse = sparse ? 1 : 0;
-  S->n_chunks = (n + C - 1) / C;
-  const int sink_keys = a->sink < n ? a->sink : n;
-  S->n_sink_chunks = (sink_keys + C - 1) / C;
-  int fw = (n - a->window) / C;
-  if (fw < S->n_sink_chunks) fw = S->n_sink_chunks;
-  S->first_window_chunk = fw;
-  if (!sparse || all_sparse) S->n_launched = S->n_chunks;
-  else S->n_launched = S->n_sink_chunks + (S->n_chunks - fw);
-  if (sparse && a->n_keys_dev) {
-    // device key count: the window's chunks are placed on the device, so launch
-    // enough for any count up to the capacity (the sink chunks, then the window
-    // span plus one chunk of misalignment; with every key sparse the same
-    // number covers [0, sink + window))
-    const int span = S->n_sink_chunks + (a->window + C - 1) / C + 1;
-    S->n_launched = span < S->n_chunks ? span : S->n_chunks;
-  }
+  S->n_chunks = (int)((n + C - 1) / C);
+  S->n_sink_chunks = (int)((sink + C - 1) / C);
+  const int span = S->n_sink_chunks + (int)((window + C - 1) / C);
+  S->n_launched = (!sparse || n <= sink + window) ? S->n_chunks : span;
+  if (S->n_launched < 1) S->n_launched = 1;  // no sparse keys: one empty partial
   S->partials = nullptr;
+}
+
+// Sparse chunk: the shortest multiple of the 64-key stage whose sink and
+// window chunks fit one thread-block cluster of DEC_CLUSTER_TARGET CTAs (merged
+// in-cluster, one launch per step), if that chunk is at most
+// DEC_SPARSE_CLUSTER_CHUNK_MAX keys; otherwise DEC_SPARSE_CHUNK with the merge
+// kernel.  A function of (sink, window) only, so anchor and non-anchor steps,
+// and host and device key counts, chunk the sparse set alike.
+static int decode_sparse_chunk(const dta_decode_args* a) {
+  const long long sink = decode_sink(a), window = decode_window(a);
+  for (int C = 64; C <= dta::DEC_SPARSE_CLUSTER_CHUNK_MAX; C += 64)
+    if ((sink + C - 1) / C + (window + C - 1) / C <= dta::DEC_CLUSTER_TARGET) return C;
+  return dta::DEC_SPARSE_CHUNK;
 }
 
 // Dense chunk for `sms` SMs (0: the shortest chunk, whose partials bound the
@@ -586,12 +600,12 @@ static int decode_setup(const dta_decode_args* a, dta::DecodeParams* p, int sms)
   p->B = a->batch; p->H = a->n_heads; p->Hkv = a->n_kv_heads; p->G = a->n_heads / a->n_kv_heads;
   p->n_keys = n;
   p->scale_log2 = a->scaling * 1.4426950408889634f;
-  p->window = a->window; p->sink = a->sink;
+  p->window = (int)decode_window(a); p->sink = (int)decode_sink(a);
   p->n_keys_dev = a->n_keys_dev;
   // with a device key count the kernels decide this per call
-  p->all_sparse = (!a->n_keys_dev && n <= a->sink + a->window) ? 1 : 0;
-  decode_chunking(a, decode_dense_chunk(a, sms), false, p->all_sparse != 0, &p->set[0]);
-  decode_chunking(a, dta::DEC_SPARSE_CHUNK, true, p->all_sparse != 0, &p->set[1]);
+  p->all_sparse = (!a->n_keys_dev && n <= (long long)p->sink + p->window) ? 1 : 0;
+  decode_chunking(a, decode_dense_chunk(a, sms), false, &p->set[0]);
+  decode_chunking(a, decode_sparse_chunk(a), true, &p->set[1]);
   return DTA_OK;
 }
 

@@ -26,6 +26,10 @@
 #ifndef DTA_DEC_PDL_MERGE
 #define DTA_DEC_PDL_MERGE 2
 #endif
+// 1: the sparse set merges in-cluster (one launch for a sparse-only step)
+#ifndef DTA_DEC_SPARSE_CLUSTER
+#define DTA_DEC_SPARSE_CLUSTER 1
+#endif
 
 namespace dta {
 
@@ -41,40 +45,46 @@ __device__ __forceinline__ int dec_n_keys(const DecodeParams& p) {
 }
 template <bool DEVN>
 __device__ __forceinline__ bool dec_all_sparse(const DecodeParams& p, int n) {
-  if constexpr (DEVN) return n <= p.sink + p.window;
+  if constexpr (DEVN) return (long long)n <= (long long)p.sink + p.window;
   return p.all_sparse != 0;
 }
 
-__device__ __forceinline__ bool dec_sparse_key(const DecodeParams& p, bool all_sparse, int n, int j) {
-  return all_sparse || j < p.sink || j >= n - p.window;
+// Key range [k0, k1) of launched chunk x of the sparse set with n live keys:
+// [0, sink) and then [n - window, n) tiled from each range's first key, or
+// [0, n) when every key is sparse.  An empty range leaves an empty partial.
+__device__ __forceinline__ void dec_sparse_range(const DecodeParams& p, const DecodeSet& S, bool all_sparse, int n,
+                                                 int x, int& k0, int& k1) {
+  if (all_sparse) {
+    k0 = x * S.chunk;
+    k1 = min(k0 + S.chunk, n);
+  } else if (x >= S.n_sink_chunks) {
+    k0 = n - p.window + (x - S.n_sink_chunks) * S.chunk;
+    k1 = min(k0 + S.chunk, n);
+  } else {
+    k0 = x * S.chunk;
+    k1 = min(k0 + S.chunk, p.sink);
+  }
 }
 
-template <bool DEVN>
-__device__ __forceinline__ int dec_chunk_of_block(const DecodeParams& p, const DecodeSet& S, bool all_sparse, int n,
-                                                  int x) {
-  if (!S.sparse || all_sparse) return x;
-  // window chunks start at the chunk holding key n - window, after the sink chunks
-  int fwc = S.first_window_chunk;
-  if constexpr (DEVN) fwc = max(S.n_sink_chunks, max(n - p.window, 0) / S.chunk);
-  return x < S.n_sink_chunks ? x : fwc + (x - S.n_sink_chunks);
-}
-
+// Kinds of partial launch: the dense set (partials to the merge kernel), the
+// sparse set (likewise), the sparse set merged in-cluster.
+constexpr int DEC_DENSE = 0, DEC_SPARSE = 1, DEC_SPARSE_CLU = 2;
 
 // ---------------------------------------------------------------------------
 // Tensor-core partial kernel.  CTA = (chunk of S.chunk keys, batch x KV
 // group, key set), 4 warps.  The chunk's K and V rows stream through shared
 // memory in 64-key stages (cp.async, 16-byte chunks XOR-swizzled by row so
-// ldmatrix is conflict-free, two stages in flight).  Warp w owns keys
+// ldmatrix is conflict-free, DEC_NSTAGE stages in flight).  Warp w owns keys
 // [16w, 16w + 16) of every stage and runs, per stage, S = Q K^T and O += P V
 // with mma.sync m16n8k16 (bf16 in, fp32 accumulate): the M = 16 rows are the
 // G <= 8 query heads of the group (rows >= G are zero), N runs over keys for
 // S and over head dims for O, and the S accumulator fragments become the P
 // operand fragments in registers.  An online softmax (running max and sum per
 // head, exact rescale) runs on the fragments; the four warps' states are
-// merged once per chunk.  `which` selects the key set and its chunking:
-// 0 = dense (every key, long chunks), 1 = sparse (sink + window, short
-// chunks); an anchor step launches both, and the sparse launch re-reads only
-// the few sink and window chunks (from L2).
+// merged once per chunk.  KIND selects the key set and its chunking: the
+// dense set (every key, long chunks) or the sparse set (sink + window, short
+// chunks holding only sparse keys); an anchor step launches both, and the
+// sparse launch re-reads the sink and window keys (from L2).
 // ---------------------------------------------------------------------------
 constexpr int DEC_STAGE = 64;  // keys per shared-memory stage
 #ifndef DTA_DEC_NSTAGE
@@ -102,8 +112,12 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
-template <int HD, bool DEVN>
-__global__ void __launch_bounds__(DEC_THREADS) decode_mma_kernel(const __grid_constant__ DecodeParams p, int which) {
+// DEC_SPARSE_CLU: the grid's x extent is one thread-block cluster per (batch,
+// group) and the chunks' partials merge through distributed shared memory
+// instead of the merge kernel (the sparse set when its chunks fit one cluster).
+template <int HD, bool DEVN, int KIND>
+__global__ void __launch_bounds__(DEC_THREADS) decode_mma_kernel(const __grid_constant__ DecodeParams p) {
+  constexpr bool CLU = KIND == DEC_SPARSE_CLU;
   constexpr int CH = HD / 8;                  // 16-byte chunks per row
   constexpr int ROWB = HD * 2;                // bytes per K/V row
   constexpr int STAGE_BYTES = DEC_STAGE * ROWB;
@@ -115,17 +129,20 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_mma_kernel(const __grid_co
   // lets a programmatic dependent merge launch start its CTAs now; they wait
   // in griddepcontrol.wait for this grid's completion and its memory flush
   grid_dependents_launch();
-  const DecodeSet& S = p.set[which];
+  const DecodeSet& S = p.set[KIND == DEC_DENSE ? 0 : 1];
   const int n_live = dec_n_keys<DEVN>(p);
-  const bool all_sparse = dec_all_sparse<DEVN>(p, n_live);
-  const int c = dec_chunk_of_block<DEVN>(p, S, all_sparse, n_live, blockIdx.x);
+  int k0, k1;
+  if constexpr (KIND == DEC_DENSE) {
+    k0 = blockIdx.x * S.chunk;
+    k1 = min(k0 + S.chunk, n_live);
+  } else {
+    dec_sparse_range(p, S, dec_all_sparse<DEVN>(p, n_live), n_live, blockIdx.x, k0, k1);
+  }
   const int bg = blockIdx.y;
   const int b = bg / p.Hkv, g = bg - (bg / p.Hkv) * p.Hkv;
   const int G = p.G;
-  const int k0 = c * S.chunk;
-  const int k1 = min(k0 + S.chunk, n_live);
-  // (device count: a chunk past the live keys has none and leaves an empty partial)
-  const int nk = DEVN ? max(k1 - k0, 0) : k1 - k0;
+  // (a chunk past the live keys of a device count has none and leaves an empty partial)
+  const int nk = (KIND == DEC_DENSE && !DEVN) ? k1 - k0 : max(k1 - k0, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gr = lane >> 2, cq = lane & 3;  // fragment row (= head) and column pair
   float* part0 = S.partials + ((long long)(b * p.H + g * G) * S.n_launched + blockIdx.x) * (4 + HD);
@@ -200,10 +217,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_mma_kernel(const __grid_co
     const int jb = s * DEC_STAGE + r0;  // chunk-local key of fragment column 0
     const int jk[4] = {jb + 2 * cq, jb + 2 * cq + 1, jb + 8 + 2 * cq, jb + 9 + 2 * cq};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const bool v = jk[e] < nk && (!S.sparse || dec_sparse_key(p, all_sparse, n_live, k0 + jk[e]));
-      sv[e] = v ? sv[e] : -INFINITY;
-    }
+    for (int e = 0; e < 4; ++e) sv[e] = jk[e] < nk ? sv[e] : -INFINITY;
     float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
@@ -252,6 +266,8 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_mma_kernel(const __grid_co
     red_o[(warp * 8 + gr) * HD + t * 8 + 2 * cq + 1] = o[t][1];
   }
   __syncthreads();
+  float* cl_o = red_ml + 4 * 2 * 8;  // CLU: this chunk's partial [8][HD], then (m, l) [2][8]
+  float* cl_ml = cl_o + 8 * HD;
   for (int idx = threadIdx.x; idx < G * HD; idx += DEC_THREADS) {
     const int h = idx / HD, t = idx - (idx / HD) * HD;
     float M = -INFINITY;
@@ -268,17 +284,74 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_mma_kernel(const __grid_co
         L += red_ml[(w * 2 + 1) * 8 + h] * sc;
       }
     }
-    float* part = part0 + h * hstride;
-    part[4 + t] = O;
-    if (t == 0) {
-      part[0] = M;
-      part[1] = L;
+    if constexpr (CLU) {
+      cl_o[h * HD + t] = O;
+      if (t == 0) {
+        cl_ml[h] = M;
+        cl_ml[8 + h] = L;
+      }
+    } else {
+      float* part = part0 + h * hstride;
+      part[4 + t] = O;
+      if (t == 0) {
+        part[0] = M;
+        part[1] = L;
+      }
     }
+  }
+  if constexpr (CLU) {
+    // every chunk's partial is in its CTA's shared memory; the cluster's CTAs
+    // split the group's G * HD outputs and merge the chunks in rank (= chunk)
+    // order with the log-sum-exp rule of the merge kernel
+    __syncwarp();
+    cluster_sync();
+    const int nct = (int)cluster_nctarank(), rank = (int)cluster_ctarank();
+    const uint32_t o_addr = smem_u32(cl_o), ml_addr = smem_u32(cl_ml);
+    // host key count with n <= sink + window: the sparse set is the dense set too
+    __nv_bfloat16* dense_dst = (!DEVN && p.all_sparse) ? p.dense_out : nullptr;
+    for (int idx = rank * DEC_THREADS + threadIdx.x; idx < G * HD; idx += nct * DEC_THREADS) {
+      const int h = idx / HD, t = idx - (idx / HD) * HD;
+      float mv[DEC_CLUSTER_MAX];
+#pragma unroll
+      for (int r = 0; r < DEC_CLUSTER_MAX; ++r)
+        mv[r] = r < nct ? ld_dsmem_f32(dsmem_addr(ml_addr + 4u * h, r)) : -INFINITY;
+      float M = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < DEC_CLUSTER_MAX; ++r) M = fmaxf(M, mv[r]);
+      float L = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+        float lv[DEC_CLUSTER_MAX], ov[DEC_CLUSTER_MAX];
+#pragma unroll
+        for (int r = 0; r < DEC_CLUSTER_MAX; ++r) {
+          const bool live = mv[r] != -INFINITY;
+          lv[r] = live ? ld_dsmem_f32(dsmem_addr(ml_addr + 4u * (8 + h), r)) : 0.f;
+          ov[r] = live ? ld_dsmem_f32(dsmem_addr(o_addr + 4u * (h * HD + t), r)) : 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < DEC_CLUSTER_MAX; ++r) {
+          if (mv[r] == -INFINITY) continue;
+          const float w = fast_exp2(mv[r] - M);
+          L += lv[r] * w;
+          O += ov[r] * w;
+        }
+      }
+      const __nv_bfloat16 o16 = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+      const long long off = ((long long)b * p.H + g * G + h) * HD + t;
+      if (p.sparse_out) p.sparse_out[off] = o16;
+      if (dense_dst) dense_dst[off] = o16;
+    }
+    __syncwarp();
+    cluster_sync();  // no CTA exits while a peer may still read its partial
   }
 }
 
-// Merge the partials of every launched chunk of a key set: grid (B*H), block HD.
-// Chunk statistics are read in batches of 8 independent loads.
+// Merge the partials of every launched chunk of a key set: grid (B*H), block
+// HD.  One pass with a running rescale: each tile of DEC_MERGE_TILE partials
+// issues all its loads (the (m, l) pair, the same address for every thread,
+// and the thread's column of o) before any is used, so a key set of up to
+// DEC_MERGE_TILE chunks costs one round trip to L2.
+constexpr int DEC_MERGE_TILE = 16;
+
 template <int HD, bool DEVN>
 __global__ void decode_merge_kernel(const __grid_constant__ DecodeParams p) {
   const int bh = blockIdx.x;
@@ -286,48 +359,46 @@ __global__ void decode_merge_kernel(const __grid_constant__ DecodeParams p) {
   grid_dependency_wait();  // no-op unless launched as a programmatic dependent
   for (int out = 0; out < 2; ++out) {
     __nv_bfloat16* dst = out == 0 ? p.dense_out : p.sparse_out;
-    if (!dst) continue;
+    if (!dst || (out == 1 && p.sparse_merged)) continue;
     // with n <= sink + window the two key sets coincide: both outputs come
     // from the sparse set's partials (host key count; with a device count the
     // dense output keeps the dense set, which covers the same keys)
     const DecodeSet& S = p.set[DEVN ? out : (out == 1 || p.all_sparse) ? 1 : 0];
     const float* base = S.partials + (long long)bh * S.n_launched * (4 + HD);
-    float M = -INFINITY;
-    for (int x0 = 0; x0 < S.n_launched; x0 += 8) {
-      float mv[8];
+    float M = -INFINITY, L = 0.f, O = 0.f;
+    for (int x0 = 0; x0 < S.n_launched; x0 += DEC_MERGE_TILE) {
+      float mv[DEC_MERGE_TILE], lv[DEC_MERGE_TILE], ov[DEC_MERGE_TILE];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < DEC_MERGE_TILE; ++u) {
         const int x = x0 + u;
-        mv[u] = x < S.n_launched ? base[(long long)x * (4 + HD)] : -INFINITY;
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) M = fmaxf(M, mv[u]);
-    }
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
-      for (int x0 = 0; x0 < S.n_launched; x0 += 8) {
-        float mv[8], lv[8], ov[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int x = x0 + u;
-          if (x < S.n_launched) {
-            const float* part = base + (long long)x * (4 + HD);
-            mv[u] = part[0];
-            lv[u] = part[1];
-            ov[u] = part[4 + t];
-          } else {
-            mv[u] = -INFINITY;
-            lv[u] = ov[u] = 0.f;
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          if (mv[u] == -INFINITY) continue;
-          const float w = fast_exp2(mv[u] - M);
-          L += lv[u] * w;
-          O += ov[u] * w;
+        if (x < S.n_launched) {
+          const float* part = base + (long long)x * (4 + HD);
+          const float2 ml = *reinterpret_cast<const float2*>(part);
+          mv[u] = ml.x;
+          lv[u] = ml.y;
+          ov[u] = part[4 + t];
+        } else {
+          mv[u] = -INFINITY;
+          lv[u] = ov[u] = 0.f;
         }
       }
+      float mt = M;
+#pragma unroll
+      for (int u = 0; u < DEC_MERGE_TILE; ++u) mt = fmaxf(mt, mv[u]);
+      if (mt == -INFINITY) continue;
+      if (M != -INFINITY) {
+        const float sc = fast_exp2(M - mt);
+        L *= sc;
+        O *= sc;
+      }
+#pragma unroll
+      for (int u = 0; u < DEC_MERGE_TILE; ++u) {
+        if (mv[u] == -INFINITY) continue;
+        const float w = fast_exp2(mv[u] - mt);
+        L += lv[u] * w;
+        O += ov[u] * w;
+      }
+      M = mt;
     }
     const float o = L > 0.f ? O / L : 0.f;
     const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
@@ -335,36 +406,96 @@ __global__ void decode_merge_kernel(const __grid_constant__ DecodeParams p) {
   }
 }
 
-template <int HD>
-static cudaError_t launch_hd(const DecodeParams& p, cudaStream_t stream) {
+// Whether `nct` CTAs of the CLU kernel fit one cluster on this device (cached
+// per size: cudaOccupancyMaxActiveClusters > 0).
+template <int HD, bool DEVN>
+static bool cluster_fits(int nct, int smem) {
+  static int fits[DEC_CLUSTER_MAX + 1] = {};  // 0 unknown, 1 yes, 2 no
+  if (nct < 1 || nct > DEC_CLUSTER_MAX) return false;
+  if (fits[nct] == 0) {
+    auto kernel = decode_mma_kernel<HD, DEVN, DEC_SPARSE_CLU>;
+    int n = 0;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess && nct > 8) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(nct);
+      cfg.blockDim = dim3(DEC_THREADS);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = nct;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+    }
+    if (e != cudaSuccess) (void)cudaGetLastError();  // a refused size is not an error of the call
+    fits[nct] = (e == cudaSuccess && n > 0) ? 1 : 2;
+  }
+  return fits[nct] == 1;
+}
+
+template <int HD, bool DEVN>
+static cudaError_t launch_hd(const DecodeParams& p_in, cudaStream_t stream) {
   constexpr int smem = DEC_NSTAGE * 2 * DEC_STAGE * HD * 2;
-  static_assert(smem >= (4 * 8 * HD + 4 * 2 * 8) * 4, "merge buffers fit in the stage buffers");
-  auto kernel = p.n_keys_dev ? decode_mma_kernel<HD, true> : decode_mma_kernel<HD, false>;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
+  static_assert(smem >= (4 * 8 * HD + 4 * 2 * 8 + 8 * HD + 2 * 8) * 4, "merge buffers fit in the stage buffers");
+  DecodeParams p = p_in;
   const bool dense_set = p.dense_out && !p.all_sparse;
   const bool sparse_set = p.sparse_out || p.all_sparse;
-  if (dense_set) kernel<<<dim3(p.set[0].n_launched, p.B * p.Hkv), DEC_THREADS, smem, stream>>>(p, 0);
-  if (sparse_set) kernel<<<dim3(p.set[1].n_launched, p.B * p.Hkv), DEC_THREADS, smem, stream>>>(p, 1);
-  const bool pdl = DTA_DEC_PDL_MERGE == 2 || (DTA_DEC_PDL_MERGE == 1 && !dense_set);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.B * p.H);
-  cfg.blockDim = dim3(HD);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  e = p.n_keys_dev ? cudaLaunchKernelEx(&cfg, decode_merge_kernel<HD, true>, p)
-                   : cudaLaunchKernelEx(&cfg, decode_merge_kernel<HD, false>, p);
-  if (e != cudaSuccess) return e;
+  const int nct = p.set[1].n_launched;
+  const bool clu = DTA_DEC_SPARSE_CLUSTER && sparse_set && cluster_fits<HD, DEVN>(nct, smem);
+  p.sparse_merged = clu ? 1 : 0;
+  cudaError_t e;
+  if (dense_set) {
+    auto kernel = decode_mma_kernel<HD, DEVN, DEC_DENSE>;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    kernel<<<dim3(p.set[0].n_launched, p.B * p.Hkv), DEC_THREADS, smem, stream>>>(p);
+  }
+  if (sparse_set && clu) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nct, p.B * p.Hkv);
+    cfg.blockDim = dim3(DEC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = nct;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, decode_mma_kernel<HD, DEVN, DEC_SPARSE_CLU>, p);
+    if (e != cudaSuccess) return e;
+  } else if (sparse_set) {
+    auto kernel = decode_mma_kernel<HD, DEVN, DEC_SPARSE>;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    kernel<<<dim3(nct, p.B * p.Hkv), DEC_THREADS, smem, stream>>>(p);
+  }
+  // the merge kernel: the dense set's output, and the sparse set's unless merged in-cluster
+  if (dense_set || !clu) {
+    const bool pdl = DTA_DEC_PDL_MERGE == 2 || (DTA_DEC_PDL_MERGE == 1 && !dense_set);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.B * p.H);
+    cfg.blockDim = dim3(HD);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    e = cudaLaunchKernelEx(&cfg, decode_merge_kernel<HD, DEVN>, p);
+    if (e != cudaSuccess) return e;
+  }
   return cudaGetLastError();
 }
 
 cudaError_t launch_decode(const DecodeParams& p, int head_dim, cudaStream_t stream) {
-  if (head_dim == 128) return launch_hd<128>(p, stream);
-  return launch_hd<64>(p, stream);
+  if (head_dim == 128) return p.n_keys_dev ? launch_hd<128, true>(p, stream) : launch_hd<128, false>(p, stream);
+  return p.n_keys_dev ? launch_hd<64, true>(p, stream) : launch_hd<64, false>(p, stream);
 }
 
 }  // namespace dta

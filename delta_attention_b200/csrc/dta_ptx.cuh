@@ -155,6 +155,35 @@ __device__ __forceinline__ void grid_dependents_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Thread-block clusters: the hardware cluster barrier (every thread of every
+// CTA arrives; release/acquire orders shared-memory writes before it with
+// distributed-shared-memory reads after it), the CTA's rank and the cluster's
+// size, and loads from a peer CTA's shared memory.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+// the shared::cluster address of `addr` (a shared::cta address) in CTA `rank`
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 // Warp-collective variant: every lane waits, then the warp reconverges so the
 // caller may issue .sync.aligned tcgen05 instructions.  The result is the
 // AND over the warp (an abort seen by any lane aborts the whole warp).
