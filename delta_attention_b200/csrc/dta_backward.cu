@@ -321,6 +321,7 @@ struct BCtrl {
   uint64_t fix_full, fix_empty;
   uint64_t st_full[2], st_empty[2];
   uint64_t s_full, p_full, acc_full, acc_empty;
+  uint64_t dp_full, ds_full;  // key-major: dP^T is in T2; dS^T has been written over it
   uint64_t k_full[3], k_empty[3], v_full[2], v_empty[2];  // query-major rings
   uint64_t s_free;      // query-major: S and dP of the iteration are in registers
   uint64_t ds_free[2];  // query-major: the dQ product has read dS buffer b
@@ -449,6 +450,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
     mbar_init(BBAR(p_full), 8);
     mbar_init(BBAR(acc_full), 1);
     mbar_init(BBAR(acc_empty), 8);
+    mbar_init(BBAR(dp_full), 1);
+    mbar_init(BBAR(ds_full), 8);
     for (int i = 0; i < 3; ++i) {
       mbar_init(BBAR(k_full[0]) + 8 * i, 1);
       mbar_init(BBAR(k_empty[0]) + 8 * i, 1);
@@ -724,37 +727,53 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
         n += T;
         ++jobs;
       } else {
-      // key-major: S^T, dP^T, then dV and dK from P^T / dS^T written over them
-      for (int u = i0; u < i1; ++u, ++n) {
-        const int st = n & 1;
-        if (!mbar_poll(BBAR(st_full[0]) + 8 * st, (n >> 1) & 1, wc, KERR_TIMEOUT_MMA)) {
-          aborted = true;
-          break;
-        }
+      // Key-major: dV(m) is issued as soon as P^T(m) has been written over
+      // S^T(m) in T1, and dK(m) once dS^T(m) is over dP^T(m) in T2, so the
+      // compute warpgroups form dS^T(m) while the pipe runs dV(m); then
+      // S^T(m + 1) and dP^T(m + 1) (the tensor pipe runs in issue order, so
+      // they overwrite T1 / T2 only after dV(m) / dK(m) have read them), and
+      // P^T(m + 1) is formed while dP^T(m + 1) runs.
+      auto issue_s = [&](int m) -> bool {  // S^T(m) = F0 . Q(m)^T into T1
+        const int st = m & 1;
+        if (!mbar_poll(BBAR(st_full[0]) + 8 * st, (m >> 1) & 1, wc, KERR_TIMEOUT_MMA)) return false;
         tc_fence_after();
-        const uint32_t s0 = str_u32 + st * G::STAGE, s1 = s0 + G::TILE;
-        const uint64_t sdesc0 = smem_desc_sw128(s0, 16, 1024), sdesc1 = smem_desc_sw128(s1, 16, 1024);
+        const uint64_t sdesc0 = smem_desc_sw128(str_u32 + st * G::STAGE, 16, 1024);
         if (elect_one()) {
-          // T1 = F0 . S0^T and T2 = F1 . S1^T (both operands K-major)
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off = ((kk >> 2) * G::REGION + (kk & 3) * 32) >> 4;
             umma_ss(tmem + G::T1, fdesc0 + off, sdesc0 + off, IDESC_SS, kk > 0 ? 1u : 0u);
           }
+          umma_commit(BBAR(s_full));
+        }
+        __syncwarp();
+        return true;
+      };
+      auto issue_dp = [&](int m, bool last_of_job) {  // dP^T(m) = F1 . dO(m)^T into T2 (stage already full)
+        const uint64_t sdesc1 = smem_desc_sw128(str_u32 + (m & 1) * G::STAGE + G::TILE, 16, 1024);
+        if (elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off = ((kk >> 2) * G::REGION + (kk & 3) * 32) >> 4;
             umma_ss(tmem + G::T2, fdesc1 + off, sdesc1 + off, IDESC_SS, kk > 0 ? 1u : 0u);
           }
-          umma_commit(BBAR(s_full));
-          if (u == i1 - 1) umma_commit(BBAR(fix_empty));
+          umma_commit(BBAR(dp_full));
+          // the job's fixed tiles are read by its S^T / dP^T products only
+          if (last_of_job) umma_commit(BBAR(fix_empty));
         }
         __syncwarp();
-        if (!mbar_poll(BBAR(p_full), n & 1, wc, KERR_TIMEOUT_MMA)) {
+      };
+      const int T = i1 - i0;
+      if (!issue_s(n)) break;
+      issue_dp(n, T == 1);
+      for (int k = 0; k < T; ++k) {
+        const int m = n + k, st = m & 1;
+        const uint32_t s0 = str_u32 + st * G::STAGE, s1 = s0 + G::TILE;
+        if (!mbar_poll(BBAR(p_full), m & 1, wc, KERR_TIMEOUT_MMA)) {
           aborted = true;
           break;
         }
-        if (u == i0 && jobs > 0 && !mbar_poll(BBAR(acc_empty), (jobs - 1) & 1, wc, KERR_TIMEOUT_MMA)) {
+        if (k == 0 && jobs > 0 && !mbar_poll(BBAR(acc_empty), (jobs - 1) & 1, wc, KERR_TIMEOUT_MMA)) {
           aborted = true;
           break;
         }
@@ -765,16 +784,37 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t acol = kk < 4 ? kk * 8 : 64 + (kk - 4) * 8;
-            const uint32_t acc = (u > i0 || kk > 0) ? 1u : 0u;
-            umma_ts(tmem + G::ACC1, tmem + G::T1 + acol, mdesc1 + ((kk * 2048) >> 4), IDESC_TS, acc);  // dV += P^T dO
-            umma_ts(tmem + G::ACC2, tmem + G::T2 + acol, mdesc0 + ((kk * 2048) >> 4), IDESC_TS, acc);  // dK += dS^T Q
+            umma_ts(tmem + G::ACC1, tmem + G::T1 + acol, mdesc1 + ((kk * 2048) >> 4), IDESC_TS,
+                    (k > 0 || kk > 0) ? 1u : 0u);  // dV += P^T dO
           }
-          umma_commit(BBAR(st_empty[0]) + 8 * st);
-          if (u == i1 - 1) umma_commit(BBAR(acc_full));
         }
         __syncwarp();
+        if (!mbar_poll(BBAR(ds_full), m & 1, wc, KERR_TIMEOUT_MMA)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        if (elect_one()) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t acol = kk < 4 ? kk * 8 : 64 + (kk - 4) * 8;
+            umma_ts(tmem + G::ACC2, tmem + G::T2 + acol, mdesc0 + ((kk * 2048) >> 4), IDESC_TS,
+                    (k > 0 || kk > 0) ? 1u : 0u);  // dK += dS^T Q
+          }
+          umma_commit(BBAR(st_empty[0]) + 8 * st);
+          if (k == T - 1) umma_commit(BBAR(acc_full));
+        }
+        __syncwarp();
+        if (k + 1 < T) {
+          if (!issue_s(m + 1)) {
+            aborted = true;
+            break;
+          }
+          issue_dp(m + 1, k + 1 == T - 1);
+        }
       }
       if (aborted) break;
+      n += T;
       ++jobs;
       }
     }
@@ -906,6 +946,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
         }
       } else
       for (int u = J.i0; u < J.i1; ++u, ++n) {
+        // key-major: P^T(u) needs S^T(u) only; dS^T(u) then needs dP^T(u)
         if (!mbar_wait_warp(BBAR(s_full), n & 1, wc, KERR_TIMEOUT_SOFTMAX)) {
           aborted = true;
           break;
@@ -913,72 +954,88 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
         tc_fence_after();
         const int st = n & 1;
         const float* stats = reinterpret_cast<const float*>(base + G::STR_OFF + st * G::STAGE + 2 * G::TILE);
-        // key-major: the query tile of this iteration
+        // the query tile of this iteration
         const int ns = J.us1 - J.us0;
-        const bool kdense = KM && u >= ns;
-        const int qt = KM ? (kdense ? J.ud0 + (u - ns) : J.us0 + u) : 0;
+        const bool kdense = u >= ns;
+        const int qt = kdense ? J.ud0 + (u - ns) : J.us0 + u;
         const int qbase = qt * p.R;
-        // query-major: the key tile of this iteration
-        const int kt = KM ? 0 : (u < J.n0 ? u : J.w0 + (u - J.n0));
+        // phase 1: P^T = exp2(S^T scale - lse) written over S^T in T1 (bf16),
+        // 32 columns at a time; P^T is kept packed for phase 2
+        const uint64_t sl2x2 = f2_pack(sl2, sl2);
+        uint32_t pk[2][16];
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int col0 = wg * 64 + c * 32;
-          float s[32], dp[32];
+          float s[32];
           tmem_ld32f(tmem + lane_off + G::T1 + col0, s);
-          tmem_ld32f(tmem + lane_off + G::T2 + col0, dp);
           tmem_wait_ld();
+          // columns col0 .. col0+31 are rows rr0 + e of the tile (two runs of 16 when R = 16)
           uint32_t m;
-          if constexpr (KM) {
-            // columns col0 .. col0+31 are rows rr0 + e of the tile (two runs of 16 when R = 16)
-            const int lo = kdense ? kfirst : klo, hi = kdense ? p.n_sel : khi;
-            if (p.R >= 32) {
-              const int b0 = qbase + (col0 & (p.R - 1));
-              m = bits_range(lo - b0, hi - b0);
-            } else {
-              const uint32_t h16 = bits_range(lo - qbase, hi - qbase) & 0xffffu;
-              m = h16 | (h16 << 16);
-            }
+          const int lo = kdense ? kfirst : klo, hi = kdense ? p.n_sel : khi;
+          if (p.R >= 32) {
+            const int b0 = qbase + (col0 & (p.R - 1));
+            m = bits_range(lo - b0, hi - b0);
           } else {
-            const int kb = kt * BWD_BN + col0;
-            m = qvalid ? bits_range(0, qpos - kb + 1) : 0u;
-            if (p.pass == BWD_SPARSE) m &= bits_range(0, p.sink - kb) | bits_range(qlo - kb, 32);
+            const uint32_t h16 = bits_range(lo - qbase, hi - qbase) & 0xffffu;
+            m = h16 | (h16 << 16);
           }
-          uint32_t pk[16], dk[16];
-          // P = exp2(s * scale - lse) and dS = P (dP - D) on packed fp32 pairs;
-          // the query rows' -lse and D come four at a time from the stage's stats
-          const uint64_t sl2x2 = f2_pack(sl2, sl2);
+          // the query rows' -lse come four at a time from the stage's stats
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
             const float4 nl4 = *reinterpret_cast<const float4*>(stats + col0 + e);
-            const float4 dd4 = *reinterpret_cast<const float4*>(stats + 128 + col0 + e);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int f = e + 2 * h;
               const uint64_t nl = h ? f2_pack(nl4.z, nl4.w) : f2_pack(nl4.x, nl4.y);
-              const uint64_t dd = h ? f2_pack(dd4.z, dd4.w) : f2_pack(dd4.x, dd4.y);
               float a0, a1;
               f2_unpack(f2_fma(f2_pack(s[f], s[f + 1]), sl2x2, nl), a0, a1);
               const float p0 = ((m >> f) & 1u) ? fast_exp2(a0) : 0.f;
               const float p1 = ((m >> (f + 1)) & 1u) ? fast_exp2(a1) : 0.f;
-              const uint64_t p2 = f2_pack(p0, p1);
-              float d0, d1;
-              f2_unpack(f2_mul(p2, f2_sub(f2_pack(dp[f], dp[f + 1]), dd)), d0, d1);
-              pk[f >> 1] = pack_bf16x2(p0, p1);
-              dk[f >> 1] = pack_bf16x2(d0, d1);
+              pk[c][f >> 1] = pack_bf16x2(p0, p1);
             }
           }
           __syncwarp();
-          if constexpr (KM) {
-            tmem_st16(tmem + lane_off + G::T1 + wg * 64 + c * 16, pk);
-            tmem_st16(tmem + lane_off + G::T2 + wg * 64 + c * 16, dk);
-          } else {
-            tmem_st16(tmem + lane_off + G::T1 + wg * 64 + c * 16, dk);
-          }
+          tmem_st16(tmem + lane_off + G::T1 + wg * 64 + c * 16, pk[c]);
         }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(BBAR(p_full));
+        // phase 2: dS^T = P^T (dP^T - D) written over dP^T in T2 (bf16), from
+        // the packed P^T (the bf16 values the dV product uses)
+        if (!mbar_wait_warp(BBAR(dp_full), n & 1, wc, KERR_TIMEOUT_SOFTMAX)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int col0 = wg * 64 + c * 32;
+          float dp[32];
+          tmem_ld32f(tmem + lane_off + G::T2 + col0, dp);
+          tmem_wait_ld();
+          uint32_t dk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            const float4 dd4 = *reinterpret_cast<const float4*>(stats + 128 + col0 + e);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int f = e + 2 * h;
+              const uint64_t dd = h ? f2_pack(dd4.z, dd4.w) : f2_pack(dd4.x, dd4.y);
+              const uint32_t pp = pk[c][f >> 1];
+              const uint64_t p2 = f2_pack(__uint_as_float(pp << 16), __uint_as_float(pp & 0xffff0000u));
+              float d0, d1;
+              f2_unpack(f2_mul(p2, f2_sub(f2_pack(dp[f], dp[f + 1]), dd)), d0, d1);
+              dk[f >> 1] = pack_bf16x2(d0, d1);
+            }
+          }
+          __syncwarp();
+          tmem_st16(tmem + lane_off + G::T2 + wg * 64 + c * 16, dk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BBAR(ds_full));
       }
       if (aborted) break;
       // ---- epilogue: this warpgroup's half of the accumulator columns ----
