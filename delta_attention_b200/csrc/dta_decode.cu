@@ -18,6 +18,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "dta_ptx.cuh"
 #include "dta_decode.h"
 
@@ -406,17 +408,34 @@ __global__ void decode_merge_kernel(const __grid_constant__ DecodeParams p) {
   }
 }
 
-// Whether `nct` CTAs of the CLU kernel fit one cluster on this device (cached
-// per size: cudaOccupancyMaxActiveClusters > 0).
+// Sets the CLU kernel's launch attributes for a cluster of `nct` CTAs on the
+// current device (the dynamic shared memory, and the non-portable cluster
+// sizes above 8).
+template <int HD, bool DEVN>
+static cudaError_t cluster_attrs(int nct, int smem) {
+  auto kernel = decode_mma_kernel<HD, DEVN, DEC_SPARSE_CLU>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess && nct > 8) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  return e;
+}
+
+// Whether `nct` CTAs of the CLU kernel fit one cluster on the current device
+// (cudaOccupancyMaxActiveClusters > 0), cached per device and size.
 template <int HD, bool DEVN>
 static bool cluster_fits(int nct, int smem) {
-  static int fits[DEC_CLUSTER_MAX + 1] = {};  // 0 unknown, 1 yes, 2 no
+  constexpr int kDevices = 64;
+  static std::mutex mu;
+  static int fits[kDevices][DEC_CLUSTER_MAX + 1] = {};  // 0 unknown, 1 yes, 2 no
   if (nct < 1 || nct > DEC_CLUSTER_MAX) return false;
-  if (fits[nct] == 0) {
-    auto kernel = decode_mma_kernel<HD, DEVN, DEC_SPARSE_CLU>;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kDevices) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (fits[dev][nct] == 0) {
     int n = 0;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e == cudaSuccess && nct > 8) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaError_t e = cluster_attrs<HD, DEVN>(nct, smem);
     if (e == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(nct);
@@ -429,12 +448,12 @@ static bool cluster_fits(int nct, int smem) {
       attr[0].val.clusterDim.z = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+      e = cudaOccupancyMaxActiveClusters(&n, decode_mma_kernel<HD, DEVN, DEC_SPARSE_CLU>, &cfg);
     }
     if (e != cudaSuccess) (void)cudaGetLastError();  // a refused size is not an error of the call
-    fits[nct] = (e == cudaSuccess && n > 0) ? 1 : 2;
+    fits[dev][nct] = (e == cudaSuccess && n > 0) ? 1 : 2;
   }
-  return fits[nct] == 1;
+  return fits[dev][nct] == 1;
 }
 
 template <int HD, bool DEVN>
@@ -455,6 +474,7 @@ static cudaError_t launch_hd(const DecodeParams& p_in, cudaStream_t stream) {
     kernel<<<dim3(p.set[0].n_launched, p.B * p.Hkv), DEC_THREADS, smem, stream>>>(p);
   }
   if (sparse_set && clu) {
+    if ((e = cluster_attrs<HD, DEVN>(nct, smem)) != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(nct, p.B * p.Hkv);
     cfg.blockDim = dim3(DEC_THREADS);
