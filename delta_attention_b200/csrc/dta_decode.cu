@@ -2,18 +2,19 @@
 //
 // Split-K over the cache: CTA (chunk, batch x kv-group, key set) streams its
 // chunk of K and V through shared memory once, serves every query head of the
-// GQA group with tensor-core products, and writes an unnormalised partial
+// GQA group with tensor-core products, and forms an unnormalised partial
 // (max, sum, o[d]) for its key set: DENSE (every key) or SPARSE (the first
 // `sink` keys plus the last `window` keys; delta_attention/llama.py:538-550).
-// A merge kernel combines the partials with the log-sum-exp rule.  An anchor
+// The dense set's partials go to global memory and a merge kernel combines
+// them with the log-sum-exp rule; it is a programmatic dependent launch
+// (DTA_DEC_PDL_MERGE), so its CTAs become resident while the partials run and
+// wait on the device for them.  The sparse set's chunks tile [0, sink) and
+// [n - window, n) exactly; when they fit one thread-block cluster per (batch,
+// group), the cluster merges them through distributed shared memory and a
+// sparse-only step is a single launch (DTA_DEC_SPARSE_CLUSTER).  An anchor
 // step of delta decode (delta_attention/llama.py:552-634) launches the dense
-// set's grid and then the sparse set's, whose CTAs cover only the chunks that
-// intersect the sink and window and re-read them from L2; a non-anchor step
-// launches only the sparse grid.  The merge is a programmatic dependent launch
-// (DTA_DEC_PDL_MERGE): its CTAs become resident while the partial grid runs
-// and wait on the device for it, so no step pays the merge's launch latency
-// after the partials (same-box A/B: sparse 10.75 -> 10.24 us, anchor step
-// 94.5 -> 93.6 us, dense 85.9 -> 85.7 us).
+// grid, then the sparse grid (which re-reads the sink and window from L2),
+// then the merge; a non-anchor step launches only the sparse grid.
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
