@@ -56,17 +56,18 @@ def test_decode_long_cache_uses_long_chunks():
                  "sparse decode n=131072")
 
 
-@pytest.mark.parametrize("cap,window,sink", [(6000, 2048, 128), (9000, 4096, 1024), (3000, 512, 7)])
-def test_decode_device_key_count(cap, window, sink):
+@pytest.mark.parametrize("cap,window,sink,d,b", [(6000, 2048, 128, 128, 1), (9000, 4096, 1024, 128, 1),
+                                                 (3000, 512, 7, 128, 1), (5000, 1000, 64, 64, 2)])
+def test_decode_device_key_count(cap, window, sink, d, b):
     """The live key count read on the device (``n_keys_dev``, the CUDA-graph
     decode path) over a cache of ``cap`` keys gives the rows of a call with
     the host count over the first n keys: the sparse rows bit-identical
     (the sparse chunking depends on sink and window only), the dense rows
     within the oracle tolerance (their chunk follows the cache length)."""
     from delta_attention_b200 import ops
-    q, k, v = _inputs(cap, 16, 4, 128, seed=cap)
+    q, k, v = _inputs(cap, 16, 4, d, b, seed=cap)
     qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
-    sc = 128 ** -0.5
+    sc = d ** -0.5
     live = torch.zeros(1, dtype=torch.int32, device="cuda")
     for n in sorted({1, 100, sink + window, sink + window + 1, cap // 2, cap - 1, cap}):
         live.fill_(n)
