@@ -441,7 +441,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
     for (int i = 0; i < 2; ++i) {
       mbar_init(BBAR(job_full[0]) + 8 * i, 1);
       mbar_init(BBAR(job_empty[0]) + 8 * i, 1 + 8);  // MMA warp lane 0 + 8 compute warps
-      mbar_init(BBAR(st_full[0]) + 8 * i, 1);
+      mbar_init(BBAR(st_full[0]) + 8 * i, 2);  // the copies' expect_tx arrival + the stats' arrival
       mbar_init(BBAR(st_empty[0]) + 8 * i, 1);
     }
     mbar_init(BBAR(fix_full), 1);
@@ -582,6 +582,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
           const bool dense = u >= ns;
           const int qt = dense ? J.ud0 + (u - ns) : J.us0 + u;
           float* stats = reinterpret_cast<float*>(base + G::STR_OFF + st * G::STAGE + 2 * G::TILE);
+          // the tiles' copies first, so they are in flight while the stats are
+          // gathered; the stats then add the barrier's second arrival
+          if (lane == 0) {
+            mbar_arrive_expect_tx(BBAR(st_full[0]) + 8 * st, 2 * G::TILE);
+            for (int rg = 0; rg < G::REGIONS; ++rg) {
+              if (dense) {
+                tma_load_4d(s0 + rg * G::REGION, &p.tm_qsel, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
+                tma_load_4d(s1 + rg * G::REGION, &p.tm_gdn, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
+              } else {
+                tma_load_4d(s0 + rg * G::REGION, &p.tm_q, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
+                tma_load_4d(s1 + rg * G::REGION, &p.tm_gsp, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
+              }
+            }
+          }
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int m = lane + 32 * k;
@@ -602,18 +616,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
             stats[128 + m] = dv;
           }
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive_expect_tx(BBAR(st_full[0]) + 8 * st, 2 * G::TILE);
-            for (int rg = 0; rg < G::REGIONS; ++rg) {
-              if (dense) {
-                tma_load_4d(s0 + rg * G::REGION, &p.tm_qsel, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
-                tma_load_4d(s1 + rg * G::REGION, &p.tm_gdn, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
-              } else {
-                tma_load_4d(s0 + rg * G::REGION, &p.tm_q, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
-                tma_load_4d(s1 + rg * G::REGION, &p.tm_gsp, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
-              }
-            }
-          }
+          if (lane == 0) mbar_arrive(BBAR(st_full[0]) + 8 * st);
         }
       }
       }
