@@ -40,6 +40,10 @@ def test_decode_dense_and_sparse(n, H, Hkv, d, b, window, sink):
     none, sparse2 = ops.decode(q.cuda(), k.cuda(), v.cuda(), window=window, sink=sink, want_dense=False)
     assert none is None
     assert torch.equal(sparse2, sparse)
+    # dense only (with n <= sink + window it comes from the sparse set's launch)
+    dense2, none = ops.decode(q.cuda(), k.cuda(), v.cuda(), window=window, sink=sink, want_sparse=False)
+    assert none is None
+    assert torch.equal(dense2, dense)
 
 
 def test_decode_long_cache_uses_long_chunks():
