@@ -35,6 +35,7 @@ import json
 import math
 import os
 import statistics
+import select
 import subprocess
 import sys
 import threading
@@ -104,6 +105,7 @@ class ClockSampler:
         self.enabled = enabled
         self.proc = None
         self.out = ""
+        self.pre = ""  # the sampler's first line, taken just before the timed region
 
     def __enter__(self):
         if self.enabled:
@@ -113,28 +115,44 @@ class ClockSampler:
                      "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             except OSError:
                 self.proc = None
+            # nvidia-smi takes a few hundred ms to start: wait for its first
+            # sample, so that a short timed region is sampled from its start
+            if self.proc is not None:
+                ready, _, _ = select.select([self.proc.stdout], [], [], 5.0)
+                if ready:
+                    self.pre = self.proc.stdout.readline()
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                rest, _ = self.proc.communicate(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                self.out, _ = self.proc.communicate()
+                rest, _ = self.proc.communicate()
+            self.out = rest or ""
         return False
 
     def summary(self):
         rows = [r for r in csv.reader(io.StringIO(self.out)) if len(r) >= 9]
+        note = None
+        if not rows:
+            # a timed region shorter than the sampling interval: report the
+            # sample taken as it started
+            rows = [r for r in csv.reader(io.StringIO(self.pre)) if len(r) >= 9]
+            note = "timed region shorter than the 100 ms sampling interval; sample taken at its start"
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+               "reasons": reasons, "samples": len(rows)}
+        if note:
+            out["note"] = note
+        return out
 
 
 # ---------------------------------------------------------------------------
@@ -508,11 +526,12 @@ def run_b200(args, rank, world, local_rank):
         step()
     torch.cuda.synchronize()
     ops.check_errors()
-    if world > 1:
-        dist.barrier()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(physical_gpu(local_rank), enabled=not args.no_clocks) as clk:
+        # (the sampler is running before the barrier that starts the timed region)
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
         t_start.record()
         for i in range(args.steps):
