@@ -323,7 +323,8 @@ struct BCtrl {
   uint64_t s_full, p_full, acc_full, acc_empty;
   uint64_t dp_full, ds_full;  // key-major: dP^T is in T2; dS^T has been written over it
   uint64_t k_full[3], k_empty[3], v_full[2], v_empty[2];  // query-major rings
-  uint64_t s_free;      // query-major: S and dP of the iteration are in registers
+  uint64_t s_free;      // query-major: S of the iteration is in registers (T1 free)
+  uint64_t dp_free;     // query-major: dP of the iteration is in registers (T2 free)
   uint64_t ds_free[2];  // query-major: the dQ product has read dS buffer b
   uint64_t drain;
   // job record: [0] kind (1 job, -1 end), [1] b, [2] g, [3] tile, [4] i0,
@@ -461,6 +462,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
       mbar_init(BBAR(v_empty[0]) + 8 * i, 1);
     }
     mbar_init(BBAR(s_free), 8);
+    mbar_init(BBAR(dp_free), 8);
     mbar_init(BBAR(ds_free[0]), 1);
     mbar_init(BBAR(ds_free[0]) + 8, 1);
     mbar_init(BBAR(drain), 1);
@@ -661,10 +663,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
       if (end) break;
       if (!mbar_poll(BBAR(fix_full), jobs & 1, wc, KERR_TIMEOUT_MMA)) break;
       if constexpr (!KM) {
-        // Query-major, pipelined: S and dP of iteration m + 1 are issued as
-        // soon as the compute warpgroups hold iteration m's in registers
-        // (s_free), before dQ(m); dS(m) lives in its own TMEM buffer
-        // (DS + 64 (m & 1)), so dQ(m) and S(m + 1) do not share columns.
+        // Query-major, pipelined: S of iteration m + 1 is issued as soon as
+        // the compute warpgroups hold iteration m's S in registers (s_free)
+        // and dP(m + 1) once they hold dP(m) (dp_free), both before dQ(m);
+        // dS(m) lives in its own TMEM buffer (DS + 64 (m & 1)), so dQ(m) and
+        // S(m + 1) do not share columns.
         auto issue_ss = [&](int m) -> bool {
           const int ks = m % G::KST, vs = m % G::VST;
           if (!mbar_poll(BBAR(k_full[0]) + 8 * ks, (m / G::KST) & 1, wc, KERR_TIMEOUT_MMA)) return false;
@@ -679,12 +682,18 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
               const uint32_t off = ((kk >> 2) * G::REGION + (kk & 3) * 32) >> 4;
               umma_ss(tmem + G::T1, fdesc0 + off, sdesc0 + off, IDESC_SS, kk > 0 ? 1u : 0u);
             }
+            umma_commit(BBAR(s_full));
+          }
+          __syncwarp();
+          if (m > 0 && !mbar_poll(BBAR(dp_free), (m - 1) & 1, wc, KERR_TIMEOUT_MMA)) return false;
+          tc_fence_after();
+          if (elect_one()) {
 #pragma unroll
             for (int kk = 0; kk < HD / 16; ++kk) {
               const uint32_t off = ((kk >> 2) * G::REGION + (kk & 3) * 32) >> 4;
               umma_ss(tmem + G::T2, fdesc1 + off, sdesc1 + off, IDESC_SS, kk > 0 ? 1u : 0u);
             }
-            umma_commit(BBAR(s_full));
+            umma_commit(BBAR(dp_full));
             umma_commit(BBAR(v_empty[0]) + 8 * vs);  // V is read by dP only
           }
           __syncwarp();
@@ -894,9 +903,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
       }
       bool aborted = false;
       if constexpr (!KM) {
-        // query-major: take S and dP of the iteration into registers and
-        // release them at once (the MMA issuer starts the next iteration's S
-        // and dP), then form dS into this iteration's dS buffer
+        // query-major: take S of the iteration into registers and release
+        // it (the MMA issuer starts the next iteration's S), then dP chunk by
+        // chunk, releasing it with the second chunk (the next dP), and form
+        // dS into this iteration's dS buffer
         for (int u = J.i0; u < J.i1; ++u, ++n) {
           if (!mbar_wait_warp(BBAR(s_full), n & 1, wc, KERR_TIMEOUT_SOFTMAX)) {
             aborted = true;
@@ -910,19 +920,28 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
             break;
           }
           tc_fence_after();
-          // 32 columns at a time; S and dP are released once the second
-          // chunk is in registers (the first chunk's dS is formed meanwhile)
+          float sv[2][32];
+          tmem_ld32f(tmem + lane_off + G::T1 + wg * 64, sv[0]);
+          tmem_ld32f(tmem + lane_off + G::T1 + wg * 64 + 32, sv[1]);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(BBAR(s_free));
+          if (!mbar_wait_warp(BBAR(dp_full), n & 1, wc, KERR_TIMEOUT_SOFTMAX)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
           const uint64_t sl2x2 = f2_pack(sl2, sl2);
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            float sv[32], dv[32];
-            tmem_ld32f(tmem + lane_off + G::T1 + wg * 64 + c * 32, sv);
+            float dv[32];
             tmem_ld32f(tmem + lane_off + G::T2 + wg * 64 + c * 32, dv);
             tmem_wait_ld();
             if (c == 1) {
               tc_fence_before();
               __syncwarp();
-              if (lane == 0) mbar_arrive(BBAR(s_free));
+              if (lane == 0) mbar_arrive(BBAR(dp_free));
             }
             const int kb = kt * BWD_BN + wg * 64 + c * 32;
             uint32_t m = qvalid ? bits_range(0, qpos - kb + 1) : 0u;
@@ -932,7 +951,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
               float a0, a1;
-              f2_unpack(f2_fma(f2_pack(sv[e], sv[e + 1]), sl2x2, f2_pack(-qlse, -qlse)), a0, a1);
+              f2_unpack(f2_fma(f2_pack(sv[c][e], sv[c][e + 1]), sl2x2, f2_pack(-qlse, -qlse)), a0, a1);
               const float p0 = ((m >> e) & 1u) ? fast_exp2(a0) : 0.f;
               const float p1 = ((m >> (e + 1)) & 1u) ? fast_exp2(a1) : 0.f;
               float d0, d1;

@@ -75,7 +75,9 @@ def _tp_worker(rank, world, port, arch_name, ret):
     logits = m.logits_last(m.forward(ids)[:, -1])
     step = m.logits_last(m.forward(ids[:, :1] * 0 + 7)[:, -1])  # one cached decode position
     if rank == 0:
-        ret.put((logits, step))
+        # numpy arrays travel by value (a torch tensor would pass a shared-memory
+        # handle that must outlive this process until the parent has opened it)
+        ret.put((logits.detach().numpy().copy(), step.detach().numpy().copy()))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -88,7 +90,7 @@ def test_two_rank_tensor_parallel_matches_one_rank(arch_name):
     procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, arch_name, q)) for r in range(2)]
     for p in procs:
         p.start()
-    logits_tp, step_tp = q.get(timeout=180)
+    logits_tp, step_tp = (torch.from_numpy(a) for a in q.get(timeout=180))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
