@@ -572,54 +572,57 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
       // key-major: the streamed operand pair (q, dO tiles and their rows' lse, D)
       for (int u = J.i0; u < J.i1; ++u, ++n) {
         const int st = n & 1;
+        // query rows of this iteration: their lse and D, loaded before the
+        // wait for the ring slot so that their latency overlaps it (columns
+        // the tile does not have: lse = +inf, D = 0)
+        const int ns = J.us1 - J.us0;
+        const bool dense = u >= ns;
+        const int qt = dense ? J.ud0 + (u - ns) : J.us0 + u;
+        float lse[4], dv[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int m = lane + 32 * k;
+          const int hh = m >> r_shift, rr = m & (p.R - 1);
+          const int head = J.g * p.G + hh;
+          const int row = qt * p.R + rr;
+          lse[k] = INFINITY;
+          dv[k] = 0.f;
+          if (!dense && row < p.s_p) {
+            const long long o = ((long long)J.b * p.H + head) * p.S + row;
+            lse[k] = p.lse_sp[o];
+            dv[k] = p.d_sp[o];
+          } else if (dense && row < p.n_sel) {
+            const long long o = ((long long)J.b * p.H + head) * p.n_sel + row;
+            lse[k] = p.lse_dn[o];
+            dv[k] = p.d_dn[o];
+          }
+        }
         if (!mbar_wait_warp(BBAR(st_empty[0]) + 8 * st, ((n >> 1) & 1) ^ 1, wc, KERR_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
         }
         const uint32_t s0 = str_u32 + st * G::STAGE, s1 = s0 + G::TILE;
-        if constexpr (KM) {
-          // query rows of this iteration: their lse and D go to the stage's
-          // stats (columns the tile does not have: lse = +inf, D = 0)
-          const int ns = J.us1 - J.us0;
-          const bool dense = u >= ns;
-          const int qt = dense ? J.ud0 + (u - ns) : J.us0 + u;
-          float* stats = reinterpret_cast<float*>(base + G::STR_OFF + st * G::STAGE + 2 * G::TILE);
-          // the tiles' copies first, so they are in flight while the stats are
-          // gathered; the stats then add the barrier's second arrival
-          if (lane == 0) {
-            mbar_arrive_expect_tx(BBAR(st_full[0]) + 8 * st, 2 * G::TILE);
-            for (int rg = 0; rg < G::REGIONS; ++rg) {
-              if (dense) {
-                tma_load_4d(s0 + rg * G::REGION, &p.tm_qsel, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
-                tma_load_4d(s1 + rg * G::REGION, &p.tm_gdn, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
-              } else {
-                tma_load_4d(s0 + rg * G::REGION, &p.tm_q, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
-                tma_load_4d(s1 + rg * G::REGION, &p.tm_gsp, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
-              }
+        float* stats = reinterpret_cast<float*>(base + G::STR_OFF + st * G::STAGE + 2 * G::TILE);
+        // the tiles' copies, then the stats, which add the barrier's second arrival
+        if (lane == 0) {
+          mbar_arrive_expect_tx(BBAR(st_full[0]) + 8 * st, 2 * G::TILE);
+          for (int rg = 0; rg < G::REGIONS; ++rg) {
+            if (dense) {
+              tma_load_4d(s0 + rg * G::REGION, &p.tm_qsel, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
+              tma_load_4d(s1 + rg * G::REGION, &p.tm_gdn, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
+            } else {
+              tma_load_4d(s0 + rg * G::REGION, &p.tm_q, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
+              tma_load_4d(s1 + rg * G::REGION, &p.tm_gsp, BBAR(st_full[0]) + 8 * st, rg * 64, qt * p.R, J.g * p.G, J.b);
             }
           }
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int m = lane + 32 * k;
-            const int hh = m >> r_shift, rr = m & (p.R - 1);
-            const int head = J.g * p.G + hh;
-            const int row = qt * p.R + rr;
-            float lse = INFINITY, dv = 0.f;  // (columns the tile does not have)
-            if (!dense && row < p.s_p) {
-              const long long o = ((long long)J.b * p.H + head) * p.S + row;
-              lse = p.lse_sp[o];
-              dv = p.d_sp[o];
-            } else if (dense && row < p.n_sel) {
-              const long long o = ((long long)J.b * p.H + head) * p.n_sel + row;
-              lse = p.lse_dn[o];
-              dv = p.d_dn[o];
-            }
-            stats[m] = -lse;  // negated: the compute warps form s * scale - lse with one packed fma
-            stats[128 + m] = dv;
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(BBAR(st_full[0]) + 8 * st);
         }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          stats[lane + 32 * k] = -lse[k];  // negated: the compute warps form s * scale - lse with one packed fma
+          stats[128 + lane + 32 * k] = dv[k];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BBAR(st_full[0]) + 8 * st);
       }
       }
     }
@@ -740,11 +743,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
         ++jobs;
       } else {
       // Key-major: dV(m) is issued as soon as P^T(m) has been written over
-      // S^T(m) in T1, and dK(m) once dS^T(m) is over dP^T(m) in T2, so the
-      // compute warpgroups form dS^T(m) while the pipe runs dV(m); then
-      // S^T(m + 1) and dP^T(m + 1) (the tensor pipe runs in issue order, so
-      // they overwrite T1 / T2 only after dV(m) / dK(m) have read them), and
-      // P^T(m + 1) is formed while dP^T(m + 1) runs.
+      // S^T(m) in T1, S^T(m + 1) right behind it (the tensor pipe runs in
+      // issue order, so it overwrites T1 only after dV(m) has read it), dK(m)
+      // once dS^T(m) is over dP^T(m) in T2, then dP^T(m + 1) into the T2
+      // dK(m) has read.  The compute warpgroups thus form dS^T(m) while the
+      // pipe runs dV(m) and S^T(m + 1), and P^T(m + 1) while it runs dK(m) and
+      // dP^T(m + 1).  (The stage of m + 1 must be in place early: its rows'
+      // statistics are loaded before the producer waits for the ring slot.)
       auto issue_s = [&](int m) -> bool {  // S^T(m) = F0 . Q(m)^T into T1
         const int st = m & 1;
         if (!mbar_poll(BBAR(st_full[0]) + 8 * st, (m >> 1) & 1, wc, KERR_TIMEOUT_MMA)) return false;
@@ -801,6 +806,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
           }
         }
         __syncwarp();
+        if (k + 1 < T && !issue_s(m + 1)) {
+          aborted = true;
+          break;
+        }
         if (!mbar_poll(BBAR(ds_full), m & 1, wc, KERR_TIMEOUT_MMA)) {
           aborted = true;
           break;
@@ -817,13 +826,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) bwd_kernel(const __grid_consta
           if (k == T - 1) umma_commit(BBAR(acc_full));
         }
         __syncwarp();
-        if (k + 1 < T) {
-          if (!issue_s(m + 1)) {
-            aborted = true;
-            break;
-          }
-          issue_dp(m + 1, k + 1 == T - 1);
-        }
+        if (k + 1 < T) issue_dp(m + 1, k + 1 == T - 1);
       }
       if (aborted) break;
       n += T;
