@@ -215,3 +215,47 @@ def test_backward_workspace_size():
             + al(H * s * 4) + al(H * n_sel * 4) + al(H * n_a * d * 4) + 2 * al(Hkv * s * d * 4))
     assert L.dta_backward_workspace_size(ctypes.byref(a)) == want
     assert L.dta_backward_workspace_size(ctypes.byref(_backward_args(gamma=48))) == 0
+
+
+def _decode_args(n, H=32, Hkv=8, d=128, b=1, window=2048, sink=128, dev_count=False):
+    a = _lib.DecodeArgs()
+    a.abi_version = _lib.ABI_VERSION
+    a.batch, a.n_heads, a.n_kv_heads, a.n_keys, a.head_dim = b, H, Hkv, n, d
+    a.scaling = d ** -0.5
+    a.window, a.sink = window, sink
+    a.n_keys_dev = (1 << 20) if dev_count else None  # never dereferenced by the size query
+    return a
+
+
+def _sparse_chunk(sink, window, target=9, cmax=512, fallback=256):
+    """The sparse key set's chunk (dta_api.cu decode_sparse_chunk): the shortest
+    multiple of 64 keys whose sink and window chunks number at most `target`
+    (at most `cmax` keys), else `fallback`."""
+    for c in range(64, cmax + 1, 64):
+        if -(-sink // c) + -(-window // c) <= target:
+            return c
+    return fallback
+
+
+@pytest.mark.parametrize("n,window,sink,dev_count", [
+    (131072, 2048, 128, False),   # config 2: 256-key sparse chunks, 9 of them
+    (131072, 2048, 128, True),    # device key count: the same sparse chunking
+    (20000, 4096, 128, False),    # 512-key chunks (9)
+    (20000, 8192, 128, False),    # too long for one cluster: 256-key chunks and the merge kernel
+    (1500, 512, 1024, False),     # n <= sink + window: the sparse set tiles [0, n)
+    (600, 5000, 3, False),        # window past the cache (clamped)
+    (777, 100, 7, True),
+])
+def test_decode_workspace_size(n, window, sink, dev_count):
+    """Both key sets' partials, [b, H, launched chunks, 4 + d] fp32 each, 256-byte
+    aligned: the dense set at its shortest chunk (256 keys), the sparse set at
+    the chunking that depends on (sink, window) only."""
+    L = _lib.lib()
+    H, d = 32, 128
+    al = lambda x: (x + 255) // 256 * 256
+    s, w = min(sink, n), min(window, n)
+    dense = -(-n // 256)
+    c = _sparse_chunk(s, w)
+    sparse = -(-n // c) if n <= s + w else -(-s // c) + -(-w // c)
+    want = al(H * dense * (4 + d) * 4) + al(H * max(sparse, 1) * (4 + d) * 4)
+    assert L.dta_decode_workspace_size(ctypes.byref(_decode_args(n, window=window, sink=sink, dev_count=dev_count))) == want
