@@ -35,12 +35,13 @@
 //   backward_finalize: dK (times scale), dV to bf16
 // Per (query tile, key tile) both tcgen05 kernels run S and dP as two
 // SS-form 128 x 128 x d products and form P and dS in registers (two compute
-// warpgroups, 64 columns each, packed fp32 pairs).  Key-major: P^T and dS^T
-// go back over S^T / dP^T in TMEM as bf16 and feed TS-form products (A from
-// TMEM, B an MN-major view of the shared-memory tile that S^T and dP^T read
-// K-major).  Query-major: dS goes to one of two spare TMEM buffers, so the
-// next key tile's S and dP are issued as soon as this tile's are in registers
-// and run while dS is formed.
+// warpgroups, 64 columns each, packed fp32 pairs).  Key-major: P^T and then
+// dS^T go back over S^T / dP^T in TMEM as bf16, in two phases with their own
+// barriers, and feed TS-form products (A from TMEM, B an MN-major view of the
+// shared-memory tile that S^T and dP^T read K-major); the issue order dV,
+// next S^T, dK, next dP^T overlaps each phase with tensor work.  Query-major:
+// dS goes to one of two spare TMEM buffers, and the next key tile's S and dP
+// are issued as soon as this tile's S, respectively dP, is in registers.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
